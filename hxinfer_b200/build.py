@@ -1,0 +1,77 @@
+"""Build libhxkv.so (the sm_100a kernels + C ABI) in-tree with nvcc.
+
+    python -m hxinfer_b200.build          # or hxinfer_b200.build.build()
+
+Each .cu file under csrc/ is compiled for sm_100a only
+(-gencode arch=compute_100a,code=sm_100a) with -lineinfo; the CUDA runtime is
+linked statically so the library does not depend on which libcudart the
+process already has loaded.  Objects are rebuilt when a source or header is
+newer than its object.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+OBJ = os.path.join(PKG, "_build")
+LIB = os.path.join(PKG, "libhxkv.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-ffp-contract=off", "-Xptxas", "-warn-spills",
+              f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _newer(src_files, target) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in src_files)
+
+
+def build(verbose: bool = False, ptxas_info: bool = False) -> str:
+    os.makedirs(OBJ, exist_ok=True)
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) + \
+        glob.glob(os.path.join(ROOT, "include", "*.h"))
+    objs = []
+    for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
+        obj = os.path.join(OBJ, os.path.basename(src) + ".o")
+        objs.append(obj)
+        if not (_newer([src] + headers, obj) or ptxas_info):
+            continue
+        cmd = [nvcc()] + ARCH + NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_info else []) + \
+            ["-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0 or verbose or ptxas_info:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src}")
+    if _newer(objs, LIB):
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lpthread"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("link of libhxkv.so failed")
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv)
+    print(LIB)

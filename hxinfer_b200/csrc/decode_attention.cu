@@ -1,0 +1,689 @@
+// decode_attention.cu — K2: split-K (flash-decoding) GQA/MHA decode attention
+// over the paged head-major KV cache, plus its combine step.
+//
+// Replaces attention_score_kernel(_fp16) (hxinfer-engine/src/op/cuda/
+// attention_score_cuda.cu:17-83, 95-161): there one CTA per q head walks all
+// positions with scores staged in shared memory (so it cannot run past ~12k
+// positions) and re-reads K/V once per q head.  Here:
+//
+//  * Work is the flat list of 64-position tiles over all (sequence, kv head)
+//    segments; CTA c of C (one per SM) takes tiles [c*T/C, (c+1)*T/C), so
+//    every CTA streams the same number of bytes whatever the lengths.
+//  * Warp 4 (producer) streams each tile's K and V (2 x 16 KiB) with TMA
+//    (cp.async.bulk.tensor, 64x64 boxes, 128-byte swizzle, L2 evict-first)
+//    into a 6-stage mbarrier ring; no multicast.
+//  * Warps 0-3 (consumers) each own 16 positions of every tile.  The whole
+//    GQA group of q heads is packed into the rows of one mma.sync
+//    m16n8k16 tile, so each K/V tile is read from HBM once per group; scores
+//    and P.V accumulate in fp32; the softmax is online (running max and sum
+//    per row, warp-shuffle reductions inside each quad).
+//  * At the end of each piece (the part of a segment inside one CTA) the four
+//    warps merge in shared memory.  A piece that is a whole segment writes
+//    the normalised output; otherwise it writes (O, m, l) to a workspace slot
+//    and the combine kernel merges the pieces by log-sum-exp.
+//
+// Workspace slots: slot (seq*hkv + kv_head) holds the piece that starts at a
+// segment's first tile; slot (n_segments + c) holds CTA c's first piece when
+// that piece starts inside a segment.  So slots = n_segments + C.
+#include <cfloat>
+
+#include "hx_common.cuh"
+
+namespace hx {
+
+constexpr int kDecStages = 6;
+constexpr int kDecConsumerWarps = 4;
+constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
+constexpr int kHalfTileBytes = 64 * 64 * 2;       // one 64x64 fp16 TMA box
+constexpr int kTileBytes = 2 * kHalfTileBytes;     // 64 positions x 128 dims
+constexpr uint32_t kStageTxBytes = 2 * kTileBytes; // K + V
+
+struct DecodeParams {
+    KVView view;
+    const void* q;             // [n_seqs][hq*128], fp16 or fp32
+    const int32_t* seq_ids;
+    const int32_t* lengths;
+    int n_seqs, hq, group, q_f32;
+    float scale_log2;          // softmax scale * log2(e)
+    void* out;                 // [n_seqs][hq*128]
+    int out_f32;
+    float* ws_o;               // [slots][group][128]
+    float2* ws_ml;             // [slots][group] (m, l)
+    int* status;
+};
+
+template <int ROWS>
+struct DecodeSmem {
+    uint8_t stage[kDecStages][2][kTileBytes];  // [stage][K|V]: two 64x64 boxes each
+    float merge_o[kDecConsumerWarps][ROWS][128];
+    float merge_m[kDecConsumerWarps][ROWS];
+    float merge_l[kDecConsumerWarps][ROWS];
+    uint64_t full[kDecStages];
+    uint64_t empty[kDecStages];
+    long long sched[4];        // first seq index, kv head, tile, tile count
+};
+
+__device__ __forceinline__ int tiles_of(int len) { return (len + kBlockTokens - 1) / kBlockTokens; }
+
+__device__ __forceinline__ int clamp_len(int len, int cap) { return len < 0 ? 0 : (len > cap ? cap : len); }
+
+// Position of the CTA's tile range within the segment list.
+struct Cursor {
+    int s, h, j, tiles, len, seq;
+};
+
+__device__ __forceinline__ void cursor_load(Cursor& c, const DecodeParams& p, int s)
+{
+    c.s = s;
+    c.len = s < p.n_seqs ? clamp_len(p.lengths[s], p.view.capacity) : 0;
+    c.tiles = tiles_of(c.len);
+    c.seq = s < p.n_seqs ? p.seq_ids[s] : 0;
+}
+
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p)
+{
+    if (++c.j < c.tiles) return;
+    c.j = 0;
+    if (++c.h < p.view.hkv) return;
+    c.h = 0;
+    int s = c.s + 1;
+    cursor_load(c, p, s);
+    // skip empty sequences (length 0 has no tiles)
+    while (c.tiles == 0 && s < p.n_seqs) cursor_load(c, p, ++s);
+}
+
+// Warp-wide computation of the CTA's range: returns total tiles T and fills
+// the starting cursor / count.  All lanes of the calling warp participate.
+__device__ long long locate_range(const DecodeParams& p, int cta, int n_ctas, Cursor& cur,
+                                  long long& count)
+{
+    const int lane = threadIdx.x & 31;
+    const int hkv = p.view.hkv;
+    long long total = 0;
+    for (int base = 0; base < p.n_seqs; base += 32) {
+        int s = base + lane;
+        int t = s < p.n_seqs ? tiles_of(clamp_len(p.lengths[s], p.view.capacity)) : 0;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        total += t;
+    }
+    total *= hkv;
+    const long long g0 = total * cta / n_ctas, g1 = total * (cta + 1) / n_ctas;
+    count = g1 - g0;
+    cur.s = p.n_seqs;
+    cur.h = cur.j = 0;
+    if (count <= 0) return total;
+    long long run = 0;  // tiles before the current chunk
+    for (int base = 0; base < p.n_seqs; base += 32) {
+        int s = base + lane;
+        long long t = s < p.n_seqs ? (long long)tiles_of(clamp_len(p.lengths[s], p.view.capacity)) * hkv : 0;
+        long long incl = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            long long y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        unsigned hit = __ballot_sync(0xffffffffu, run + incl > g0);
+        if (hit) {
+            int src = __ffs(hit) - 1;
+            long long before = run + __shfl_sync(0xffffffffu, incl - t, src);
+            int s_hit = base + src;
+            cursor_load(cur, p, s_hit);
+            long long off = g0 - before;
+            cur.h = (int)(off / cur.tiles);
+            cur.j = (int)(off % cur.tiles);
+            return total;
+        }
+        run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    return total;
+}
+
+template <int ROWS>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    decode_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const DecodeParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = *reinterpret_cast<DecodeSmem<ROWS>*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x, n_ctas = gridDim.x;
+    const int n_seg = p.n_seqs * p.view.hkv;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecStages; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], kDecConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    if (warp == kDecConsumerWarps) {
+        Cursor c{};
+        long long count = 0;
+        locate_range(p, cta, n_ctas, c, count);
+        if (lane == 0) {
+            sm.sched[0] = c.s;
+            sm.sched[1] = c.h;
+            sm.sched[2] = c.j;
+            sm.sched[3] = count;
+        }
+    }
+    __syncthreads();
+    const long long count = sm.sched[3];
+    if (count <= 0) return;
+    Cursor cur{};
+    cursor_load(cur, p, (int)sm.sched[0]);
+    cur.h = (int)sm.sched[1];
+    cur.j = (int)sm.sched[2];
+
+    if (warp == kDecConsumerWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane != 0) return;
+        prefetch_tensormap(&tm_k);
+        prefetch_tensormap(&tm_v);
+        const uint64_t pol = l2_evict_first_policy();
+        const KVView& v = p.view;
+        for (long long i = 0; i < count; ++i) {
+            const int st = (int)(i % kDecStages);
+            const uint32_t round = (uint32_t)(i / kDecStages);
+            if (i >= kDecStages && !mbar_wait(&sm.empty[st], (round - 1) & 1)) {
+                record_status(p.status, HX_ERR_TIMEOUT);
+                return;
+            }
+            const int64_t pb = phys_block(v, cur.seq, cur.j);
+            if (pb < 0) {
+                // unmapped block: no copy is issued; the consumers still get a
+                // completed phase (stale data) and the status word records it
+                record_status(p.status, HX_ERR_CAPACITY);
+                mbar_arrive(&sm.full[st]);
+            } else {
+                const int64_t rel = (pb * v.block_stride + (int64_t)cur.h * v.head_stride) / 256;
+                const int row_k = (int)(v.k_row0 + rel), row_v = (int)(v.v_row0 + rel);
+                mbar_arrive_expect_tx(&sm.full[st], kStageTxBytes);
+                uint8_t* kd = sm.stage[st][0];
+                uint8_t* vd = sm.stage[st][1];
+                tma_load_2d(kd, &tm_k, 0, row_k, &sm.full[st], pol);
+                tma_load_2d(kd + kHalfTileBytes, &tm_k, 64, row_k, &sm.full[st], pol);
+                tma_load_2d(vd, &tm_v, 0, row_v, &sm.full[st], pol);
+                tma_load_2d(vd + kHalfTileBytes, &tm_v, 64, row_v, &sm.full[st], pol);
+            }
+            cursor_next(cur, p);
+        }
+        // Wait for the last copies to land before the CTA may exit.
+        for (long long i = count > kDecStages ? count - kDecStages : 0; i < count; ++i) {
+            const int st = (int)(i % kDecStages);
+            if (!mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1)) {
+                record_status(p.status, HX_ERR_TIMEOUT);
+                return;
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int g = lane >> 2, t4 = lane & 3;
+    const int w = warp;
+    uint32_t qa[8][4];
+    float o[16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    bool piece_from_seg_start = false;
+    const uint32_t stage_base = smem_u32(&sm.stage[0][0][0]);
+    // ldmatrix row addresses (before swizzle) for this lane
+    const int lm_mi = lane >> 3, lm_r = lane & 7;
+
+    for (long long i = 0; i < count; ++i) {
+        if (i == 0 || cur.j == 0) {
+            // new piece: load the packed GQA group of q rows for (s, h)
+            piece_from_seg_start = (cur.j == 0);
+            const int64_t qrow0 = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group) * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+                for (int hi = 0; hi < 2; ++hi) {  // row g (hi=0) or g+8 (hi=1)
+                    const int r = g + 8 * hi;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {  // dims 16kk+2t4 (+8)
+                        uint32_t val = 0;
+                        if (r < p.group && (hi == 0 || ROWS == 16)) {
+                            const int64_t idx = qrow0 + (int64_t)r * 128 + 16 * kk + 2 * t4 + 8 * half;
+                            if (p.q_f32) {
+                                const float2 f = *reinterpret_cast<const float2*>(
+                                    static_cast<const float*>(p.q) + idx);
+                                val = pack_half2(f.x, f.y);
+                            } else {
+                                val = *reinterpret_cast<const uint32_t*>(
+                                    static_cast<const __half*>(p.q) + idx);
+                            }
+                        }
+                        qa[kk][hi + 2 * half] = val;
+                    }
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+            m0 = m1 = -INFINITY;
+            l0 = l1 = 0.f;
+        }
+
+        const int st = (int)(i % kDecStages);
+        if (!mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1)) {
+            record_status(p.status, HX_ERR_TIMEOUT);
+            return;
+        }
+        const int valid = min(kBlockTokens, cur.len - cur.j * kBlockTokens);
+        const uint32_t kb = stage_base + st * 2 * kTileBytes;
+        const uint32_t vb = kb + kTileBytes;
+        const int tok0 = 16 * w;
+        if (valid < tok0 + 16) {
+            // Positions past the sequence end hold stale or out-of-range
+            // bytes; zero this warp's V rows there so 0 * garbage cannot
+            // reach the accumulators.
+            uint8_t* vrow = sm.stage[st][1];
+            const int lo = max(valid, tok0);
+            const int nchunks = (tok0 + 16 - lo) * 16;
+            for (int c = lane; c < nchunks; c += 32) {
+                const int row = lo + c / 16, chunk = c % 16;
+                *reinterpret_cast<uint4*>(vrow + (chunk >> 3) * kHalfTileBytes + row * 128 +
+                                          (chunk & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+        }
+
+        // S = Q K^T for this warp's 16 positions (two n-tiles of 8)
+        float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float sb[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        {
+            const int tok = tok0 + 8 * (lm_mi >> 1) + lm_r;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const int chunk = 2 * kk + (lm_mi & 1);
+                const uint32_t addr = kb + (chunk >> 3) * kHalfTileBytes + tok * 128 +
+                                      (((chunk & 7) ^ (tok & 7)) << 4);
+                uint32_t b00, b01, b10, b11;
+                ldmatrix_x4(b00, b01, b10, b11, addr);
+                if (kk & 1) {
+                    mma_16816(sb[0], qa[kk], b00, b01);
+                    mma_16816(sb[1], qa[kk], b10, b11);
+                } else {
+                    mma_16816(sa[0], qa[kk], b00, b01);
+                    mma_16816(sa[1], qa[kk], b10, b11);
+                }
+            }
+        }
+        float s[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int tok = tok0 + 8 * nt + 2 * t4 + (e & 1);
+                const float x = (sa[nt][e] + sb[nt][e]) * p.scale_log2;
+                s[nt][e] = tok < valid ? x : -INFINITY;
+            }
+
+        // online softmax, row g (elements 0,1) and row g+8 (elements 2,3)
+        float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        const float mn0 = fmaxf(m0, mx0);
+        const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+        const float al0 = fast_exp2(m0 - mu0);
+        float pr[2][4];
+        pr[0][0] = fast_exp2(s[0][0] - mu0);
+        pr[0][1] = fast_exp2(s[0][1] - mu0);
+        pr[1][0] = fast_exp2(s[1][0] - mu0);
+        pr[1][1] = fast_exp2(s[1][1] - mu0);
+        l0 = l0 * al0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
+        m0 = mn0;
+        float al1 = 1.f;
+        if (ROWS == 16) {
+            float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float mn1 = fmaxf(m1, mx1);
+            const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+            al1 = fast_exp2(m1 - mu1);
+            pr[0][2] = fast_exp2(s[0][2] - mu1);
+            pr[0][3] = fast_exp2(s[0][3] - mu1);
+            pr[1][2] = fast_exp2(s[1][2] - mu1);
+            pr[1][3] = fast_exp2(s[1][3] - mu1);
+            l1 = l1 * al1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+            m1 = mn1;
+        } else {
+            pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.f;
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= al0;
+            o[n][1] *= al0;
+            if (ROWS == 16) {
+                o[n][2] *= al1;
+                o[n][3] *= al1;
+            }
+        }
+        uint32_t pa[4];
+        pa[0] = pack_half2(pr[0][0], pr[0][1]);
+        pa[1] = pack_half2(pr[0][2], pr[0][3]);
+        pa[2] = pack_half2(pr[1][0], pr[1][1]);
+        pa[3] = pack_half2(pr[1][2], pr[1][3]);
+
+        // O += P V over this warp's 16 positions, 16 n-tiles of 8 dims
+        {
+            const int tok = tok0 + 8 * (lm_mi & 1) + lm_r;
+#pragma unroll
+            for (int np = 0; np < 8; ++np) {
+                const int chunk = 2 * np + (lm_mi >> 1);
+                const uint32_t addr = vb + (chunk >> 3) * kHalfTileBytes + tok * 128 +
+                                      (((chunk & 7) ^ (tok & 7)) << 4);
+                uint32_t v0, v1, v2, v3;
+                ldmatrix_x4_trans(v0, v1, v2, v3, addr);
+                mma_16816(o[2 * np], pa, v0, v1);
+                mma_16816(o[2 * np + 1], pa, v2, v3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[st]);
+
+        const bool seg_end = (cur.j == cur.tiles - 1);
+        if (seg_end || i == count - 1) {
+            // ---- merge the four warps' partials of this piece
+            float lq0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+            lq0 += __shfl_xor_sync(0xffffffffu, lq0, 2);
+            float lq1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+            lq1 += __shfl_xor_sync(0xffffffffu, lq1, 2);
+            if (g < p.group) {
+                if (t4 == 0) {
+                    sm.merge_m[w][g] = m0;
+                    sm.merge_l[w][g] = lq0;
+                }
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    sm.merge_o[w][g][8 * n + 2 * t4] = o[n][0];
+                    sm.merge_o[w][g][8 * n + 2 * t4 + 1] = o[n][1];
+                }
+            }
+            if (ROWS == 16 && g + 8 < p.group) {
+                if (t4 == 0) {
+                    sm.merge_m[w][g + 8] = m1;
+                    sm.merge_l[w][g + 8] = lq1;
+                }
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    sm.merge_o[w][g + 8][8 * n + 2 * t4] = o[n][2];
+                    sm.merge_o[w][g + 8][8 * n + 2 * t4 + 1] = o[n][3];
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+            const int d = threadIdx.x;  // 0..127
+            const bool whole = piece_from_seg_start && seg_end;
+            const int slot = piece_from_seg_start ? (cur.s * p.view.hkv + cur.h) : (n_seg + cta);
+            for (int r = 0; r < p.group; ++r) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int ww = 0; ww < kDecConsumerWarps; ++ww) M = fmaxf(M, sm.merge_m[ww][r]);
+                const float Mu = M == -INFINITY ? 0.f : M;
+                float L = 0.f, acc = 0.f;
+#pragma unroll
+                for (int ww = 0; ww < kDecConsumerWarps; ++ww) {
+                    const float wgt = fast_exp2(sm.merge_m[ww][r] - Mu);
+                    L += wgt * sm.merge_l[ww][r];
+                    acc += wgt * sm.merge_o[ww][r][d];
+                }
+                if (whole) {
+                    const float val = acc / L;
+                    const int64_t oi = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group + r) * 128 + d;
+                    if (p.out_f32)
+                        static_cast<float*>(p.out)[oi] = val;
+                    else
+                        static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+                } else {
+                    p.ws_o[((int64_t)slot * p.group + r) * 128 + d] = acc;
+                    if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+        }
+        cursor_next(cur, p);
+    }
+}
+
+// One CTA (128 threads, one per dim) per (sequence, kv head): merges the
+// pieces of segments that more than one CTA worked on.
+__global__ void __launch_bounds__(128)
+    decode_combine_kernel(const DecodeParams p, int n_ctas)
+{
+    const int seg = blockIdx.x;
+    const int s = seg / p.view.hkv, h = seg % p.view.hkv;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ long long sh[3];
+    if (warp == 0) {
+        // global tile range [a, b) of this segment and the total T
+        long long before = 0, total = 0;
+        for (int base = 0; base < p.n_seqs; base += 32) {
+            int si = base + lane;
+            long long t = si < p.n_seqs ? tiles_of(clamp_len(p.lengths[si], p.view.capacity)) : 0;
+            long long tb = si < s ? t : 0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                t += __shfl_xor_sync(0xffffffffu, t, o);
+                tb += __shfl_xor_sync(0xffffffffu, tb, o);
+            }
+            total += t;
+            before += tb;
+        }
+        if (lane == 0) {
+            const int tiles = tiles_of(clamp_len(p.lengths[s], p.view.capacity));
+            const long long a = (before * p.view.hkv) + (long long)h * tiles;
+            sh[0] = a;
+            sh[1] = a + tiles;
+            sh[2] = total * p.view.hkv;
+            if (p.lengths[s] < 1 || p.lengths[s] > p.view.capacity) record_status(p.status, HX_ERR_CAPACITY);
+        }
+    }
+    __syncthreads();
+    const long long a = sh[0], b = sh[1], T = sh[2];
+    const int d = threadIdx.x;
+    const int n_seg = p.n_seqs * p.view.hkv;
+    auto cstart = [&](long long c) { return T * c / n_ctas; };
+    if (a == b) {  // empty sequence: defined output of zeros
+        for (int r = 0; r < p.group; ++r) {
+            const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
+            if (p.out_f32) static_cast<float*>(p.out)[oi] = 0.f;
+            else static_cast<__half*>(p.out)[oi] = __float2half_rn(0.f);
+        }
+        return;
+    }
+    // CTAs whose (non-empty) range starts strictly inside (a, b)
+    long long c_lo = a * n_ctas / T;
+    bool any = false;
+    for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c)
+        if (cstart(c) > a && cstart(c + 1) > cstart(c)) { any = true; break; }
+    if (!any) return;  // one piece: the decode kernel wrote the output
+    for (int r = 0; r < p.group; ++r) {
+        float M = p.ws_ml[(int64_t)seg * p.group + r].x;
+        for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c)
+            if (cstart(c) > a && cstart(c + 1) > cstart(c))
+                M = fmaxf(M, p.ws_ml[(int64_t)(n_seg + c) * p.group + r].x);
+        float2 ml = p.ws_ml[(int64_t)seg * p.group + r];
+        float wgt = fast_exp2(ml.x - M);
+        float L = wgt * ml.y;
+        float acc = wgt * p.ws_o[((int64_t)seg * p.group + r) * 128 + d];
+        for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c) {
+            if (!(cstart(c) > a && cstart(c + 1) > cstart(c))) continue;
+            const int64_t slot = n_seg + c;
+            ml = p.ws_ml[slot * p.group + r];
+            wgt = fast_exp2(ml.x - M);
+            L += wgt * ml.y;
+            acc += wgt * p.ws_o[(slot * p.group + r) * 128 + d];
+        }
+        const float val = acc / L;
+        const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
+        if (p.out_f32) static_cast<float*>(p.out)[oi] = val;
+        else static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+    }
+}
+
+// Any head_dim (<= 256), any group: one CTA of 4 warps per (sequence, q
+// head); warps take positions round-robin, lanes take dims; online softmax;
+// warps merge in shared memory.  Used when the TMA path does not apply.
+__global__ void __launch_bounds__(128)
+    decode_generic_kernel(const DecodeParams p)
+{
+    const int s = blockIdx.x / p.hq, qh = blockIdx.x % p.hq;
+    const int kvh = qh / p.group;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const KVView& v = p.view;
+    const int hd = v.hd;
+    const int len = clamp_len(p.lengths[s], v.capacity), seq = p.seq_ids[s];
+    constexpr int kPer = kMaxHeadDim / 32;
+    float qv[kPer], acc[kPer];
+    const int64_t qoff = ((int64_t)s * p.hq + qh) * hd;
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+        const int d = lane + 32 * e;
+        qv[e] = 0.f;
+        acc[e] = 0.f;
+        if (d < hd)
+            qv[e] = p.q_f32 ? static_cast<const float*>(p.q)[qoff + d]
+                            : __half2float(static_cast<const __half*>(p.q)[qoff + d]);
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int pos = warp; pos < len; pos += 4) {
+        const int64_t off = token_offset(v, seq, kvh, pos);
+        if (off < 0) {
+            record_status(p.status, HX_ERR_CAPACITY);
+            break;
+        }
+        const __half* kr = reinterpret_cast<const __half*>(v.k + off);
+        const __half* vr = reinterpret_cast<const __half*>(v.v + off);
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+            const int d = lane + 32 * e;
+            if (d < hd) dot += qv[e] * __half2float(kr[d]);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float sc = dot * p.scale_log2;
+        const float mn = fmaxf(m, sc);
+        const float al = fast_exp2(m - mn), pr = fast_exp2(sc - mn);
+        l = l * al + pr;
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+            const int d = lane + 32 * e;
+            acc[e] = acc[e] * al + (d < hd ? pr * __half2float(vr[d]) : 0.f);
+        }
+        m = mn;
+    }
+    __shared__ float sm_m[4], sm_l[4], sm_o[4][kMaxHeadDim];
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+        const int d = lane + 32 * e;
+        if (d < hd) sm_o[warp][d] = acc[e];
+    }
+    __syncthreads();
+    float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
+    const float Mu = M == -INFINITY ? 0.f : M;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float L = 0.f, o = 0.f;
+        for (int ww = 0; ww < 4; ++ww) {
+            const float wgt = fast_exp2(sm_m[ww] - Mu);
+            L += wgt * sm_l[ww];
+            o += wgt * sm_o[ww][d];
+        }
+        const float val = L > 0.f ? o / L : 0.f;
+        if (p.out_f32) static_cast<float*>(p.out)[qoff + d] = val;
+        else static_cast<__half*>(p.out)[qoff + d] = __float2half_rn(val);
+    }
+}
+
+static size_t decode_ws_bytes(int n_seqs, int hkv, int group, int n_ctas)
+{
+    const size_t slots = (size_t)n_seqs * hkv + n_ctas;
+    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2);
+}
+
+template <int ROWS>
+static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas,
+                         cudaStream_t stream)
+{
+    const size_t smem = sizeof(DecodeSmem<ROWS>) + 1024;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(decode_attention_kernel<ROWS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_set[dev] = true;
+    }
+    decode_attention_kernel<ROWS><<<n_ctas, kDecThreads, smem, stream>>>(c->tm_k, c->tm_v, p);
+    if (int rc = check_launch("decode_attention_kernel")) return rc;
+    decode_combine_kernel<<<p.n_seqs * p.view.hkv, 128, 0, stream>>>(p, n_ctas);
+    return check_launch("decode_combine_kernel");
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+extern "C" size_t hx_decode_workspace_bytes(const hx_kv_cache* c, int n_seqs, int num_q_heads)
+{
+    if (!c || n_seqs < 1 || num_q_heads < 1) return 0;
+    const int hkv = c->cfg.num_kv_heads;
+    const int group = num_q_heads / hkv;
+    return decode_ws_bytes(n_seqs, hkv, group < 1 ? 1 : group, num_sms());
+}
+
+extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
+                                   const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                                   int num_q_heads, float scale, void* out, int out_dtype,
+                                   void* workspace, size_t workspace_bytes, hx_stream_t stream)
+{
+    if (!c) return fail(HX_ERR_INVALID, "null cache");
+    if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
+    if (!q || !seq_ids || !lengths || !out) return fail(HX_ERR_INVALID, "null q/seq_ids/lengths/out");
+    if (n_seqs < 0) return fail(HX_ERR_INVALID, "n_seqs < 0");
+    if (n_seqs > c->cfg.max_seqs) return fail(HX_ERR_INVALID, "n_seqs %d > max_seqs %d", n_seqs, c->cfg.max_seqs);
+    const int hkv = c->cfg.num_kv_heads, hd = c->cfg.head_dim;
+    if (num_q_heads < hkv || num_q_heads % hkv)
+        return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
+    if ((q_dtype != HX_FP16 && q_dtype != HX_FP32) || (out_dtype != HX_FP16 && out_dtype != HX_FP32))
+        return fail(HX_ERR_INVALID, "q/out dtype");
+    if (n_seqs == 0) return HX_OK;
+    const int group = num_q_heads / hkv;
+    DecodeParams p{};
+    p.view = make_view(c, layer);
+    p.q = q;
+    p.q_f32 = q_dtype == HX_FP32;
+    p.seq_ids = seq_ids;
+    p.lengths = lengths;
+    p.n_seqs = n_seqs;
+    p.hq = num_q_heads;
+    p.group = group;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.out_f32 = out_dtype == HX_FP32;
+    p.status = status_word();
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool fast = c->has_tmap && hd == 128 && group <= 16;
+    if (!fast) {
+        decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
+        return check_launch("decode_generic_kernel");
+    }
+    const int n_ctas = num_sms();
+    const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
+    if (!workspace || workspace_bytes < need)
+        return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
+                    workspace_bytes, need);
+    const size_t slots = (size_t)n_seqs * hkv + n_ctas;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) +
+                                        slots * group * 128 * sizeof(float));
+    if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
+    return launch_decode<16>(c, p, n_ctas, s);
+}

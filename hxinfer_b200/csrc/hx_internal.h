@@ -1,0 +1,81 @@
+// hx_internal.h — host-side state shared by the translation units of libhxkv.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/hx_kv.h"
+
+namespace hx {
+
+constexpr int kBlockTokens = 64;  // positions per cache block
+constexpr int kMaxHeadDim = 256;
+
+// What a kernel needs to address one layer of a cache (passed by value).
+struct KVView {
+    char* k;                 // K base of this layer
+    char* v;                 // V base of this layer
+    const int32_t* table;    // [max_seqs][mbps] physical block ids; nullptr = identity
+    int32_t mbps;            // max blocks per sequence
+    int32_t hkv;             // kv heads in this cache
+    int32_t hd;              // head_dim
+    int32_t capacity;        // positions per sequence
+    int32_t max_seqs;
+    int64_t block_stride;    // bytes between physical blocks
+    int64_t head_stride;     // bytes between kv heads inside a block
+    int64_t k_row0, v_row0;  // tensor-map row (unit: hd*2 bytes) of k / v
+};
+
+}  // namespace hx
+
+struct hx_kv_cache {
+    hx_kv_config cfg{};
+    bool wrapped = false;
+    int device = 0;
+    int32_t mbps = 0;  // max blocks per sequence
+    int64_t num_blocks = 0;
+    char* pool = nullptr;
+    size_t pool_bytes = 0;
+    char* k0 = nullptr;  // layer-0 K base
+    char* v0 = nullptr;  // layer-0 V base
+    int64_t layer_stride = 0, kv_stride = 0, block_stride = 0, head_stride = 0;
+    int32_t* d_table = nullptr;
+    std::vector<int32_t> h_table;   // host mirror of the block table
+    std::vector<int32_t> n_mapped;  // blocks mapped per sequence
+    std::vector<int32_t> free_list;
+    bool has_tmap = false;
+    CUtensorMap tm_k{}, tm_v{};     // 2-D [rows][head_dim] fp16, box 64x64, 128B swizzle
+    char* tm_k_base = nullptr;
+    char* tm_v_base = nullptr;
+};
+
+struct hx_rope_table {
+    hx_rope_config cfg{};
+    float2* d_cos_sin = nullptr;  // [max_pos][head_dim/2] (cos, sin)
+    int device = 0;
+};
+
+namespace hx {
+
+// Records the message for hx_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to HX_ERR_CUDA with its message (HX_OK if none).
+int cuda_fail(cudaError_t e, const char* what);
+// Checks the launch that was just issued.
+int check_launch(const char* what);
+// Device status word of the current device (allocated on first use).
+int* status_word();
+int num_sms();
+KVView make_view(const hx_kv_cache* c, int layer);
+
+}  // namespace hx
+
+#define HX_CUDA_TRY(expr)                                            \
+    do {                                                             \
+        cudaError_t _e = (expr);                                     \
+        if (_e != cudaSuccess) return hx::cuda_fail(_e, #expr);      \
+    } while (0)

@@ -1,0 +1,214 @@
+"""Python front end of the C ABI (include/hx_kv.h) over torch device tensors.
+
+torch supplies device memory and streams only; every computation runs in
+libhxkv.so.  Names follow the reference engine: a KV cache per model holding
+every layer's K and V, RoPE at a position ("step"), decode attention over
+``pos + 1`` positions, prefix snapshots.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib
+from ._lib import HX_FP16, HX_FP32, check, load
+
+_DT = {torch.float16: HX_FP16, torch.float32: HX_FP32}
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return _DT[t.dtype]
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise ValueError("tensors must be on a CUDA device")
+            if not t.is_contiguous():
+                raise ValueError("tensors must be contiguous")
+
+
+def device_status(clear: bool = True) -> int:
+    """Device-side status word (synchronises); raises on a recorded error."""
+    rc = load().hx_device_status(1 if clear else 0)
+    return check(rc, "device status")
+
+
+def prefix_hash(tokens) -> int:
+    arr = (C.c_int32 * len(tokens))(*[int(t) for t in tokens])
+    return int(load().hx_prefix_hash(arr, len(tokens)))
+
+
+class RopeTable:
+    """Device cos/sin table of the reference RoPE (rope_cpu.cpp:22-25)."""
+
+    def __init__(self, head_dim: int, max_pos: int, theta: float, yarn: dict | None = None):
+        cfg = _lib.hx_rope_config(head_dim=head_dim, max_pos=max_pos, theta=theta,
+                                  use_yarn=1 if yarn else 0,
+                                  yarn_factor=(yarn or {}).get("factor", 1.0),
+                                  yarn_beta_fast=(yarn or {}).get("beta_fast", 32.0),
+                                  yarn_beta_slow=(yarn or {}).get("beta_slow", 1.0),
+                                  yarn_orig_max_pos=(yarn or {}).get("orig_max_pos", 4096))
+        h = C.c_void_p()
+        check(load().hx_rope_table_create(C.byref(cfg), C.byref(h)), "rope table")
+        self.handle = h
+        self.head_dim, self.max_pos, self.theta = head_dim, max_pos, theta
+
+    def close(self):
+        if self.handle:
+            load().hx_rope_table_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def rope_qk(q: torch.Tensor, k: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+            head_dim: int, step: int, table: RopeTable, stream=None):
+    """In-place RoPE of q [rows, Hq*hd] and k [rows, Hkv*hd] at position `step`."""
+    _need_cuda(q, k)
+    rows = q.numel() // (num_q_heads * head_dim)
+    check(load().hx_rope_qk(_ptr(q), _ptr(k), _dt(q), rows, num_q_heads, num_kv_heads, head_dim,
+                            step, table.handle, _stream(stream)), "rope_qk")
+
+
+class KVCache:
+    """Paged head-major fp16 KV cache for every layer of a model (or a shard)."""
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_seqs: int,
+                 max_tokens_per_seq: int, num_blocks: int = 0, *, _handle=None):
+        self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
+        self.max_seqs, self.max_tokens_per_seq = max_seqs, max_tokens_per_seq
+        if _handle is not None:
+            self.handle = _handle
+            return
+        cfg = _lib.hx_kv_config(num_layers=num_layers, num_kv_heads=num_kv_heads,
+                                head_dim=head_dim, max_seqs=max_seqs,
+                                max_tokens_per_seq=max_tokens_per_seq, num_blocks=num_blocks)
+        h = C.c_void_p()
+        check(load().hx_kv_create(C.byref(cfg), C.byref(h)), "kv create")
+        self.handle = h
+
+    @classmethod
+    def wrap(cls, k: torch.Tensor, v: torch.Tensor, num_kv_heads: int, head_dim: int,
+             capacity: int) -> "KVCache":
+        """One-layer, one-sequence cache over caller tensors (head-major inside)."""
+        _need_cuda(k, v)
+        need = num_kv_heads * capacity * head_dim * 2
+        if k.numel() * k.element_size() < need or v.numel() * v.element_size() < need:
+            raise ValueError("cache tensors too small")
+        h = C.c_void_p()
+        check(load().hx_kv_wrap(_ptr(k), _ptr(v), num_kv_heads, head_dim, capacity, C.byref(h)),
+              "kv wrap")
+        obj = cls(1, num_kv_heads, head_dim, 1, capacity, _handle=h)
+        obj._keep = (k, v)
+        return obj
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().hx_kv_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> dict:
+        inf = _lib.hx_kv_info()
+        check(load().hx_kv_get_info(self.handle, C.byref(inf)), "kv info")
+        return {f: getattr(inf, f) for f, _ in _lib.hx_kv_info._fields_}
+
+    def reserve(self, seq: int, n_tokens: int, stream=None):
+        check(load().hx_kv_reserve(self.handle, seq, n_tokens, _stream(stream)), "kv reserve")
+
+    def release(self, seq: int, stream=None):
+        check(load().hx_kv_release(self.handle, seq, _stream(stream)), "kv release")
+
+    def write(self, layer: int, seq: int, start: int, k: torch.Tensor, v: torch.Tensor,
+              stream=None):
+        _need_cuda(k, v)
+        n = k.numel() // (self.num_kv_heads * self.head_dim)
+        check(load().hx_kv_write(self.handle, layer, seq, start, n, _ptr(k), _ptr(v), _dt(k),
+                                 _stream(stream)), "kv write")
+
+    def read(self, layer: int, seq: int, start: int, n: int, stream=None):
+        dev = torch.device("cuda", torch.cuda.current_device())
+        k = torch.empty((n, self.num_kv_heads, self.head_dim), dtype=torch.float16, device=dev)
+        v = torch.empty_like(k)
+        check(load().hx_kv_read(self.handle, layer, seq, start, n, _ptr(k), _ptr(v),
+                                _stream(stream)), "kv read")
+        return k, v
+
+    def fill_normal(self, seed: int, stream=None):
+        check(load().hx_kv_fill_normal(self.handle, seed & (2**64 - 1), _stream(stream)),
+              "kv fill")
+
+    def rope_append(self, layer: int, k: torch.Tensor, v: torch.Tensor, seq_ids: torch.Tensor,
+                    positions: torch.Tensor, *, q: torch.Tensor | None = None,
+                    num_q_heads: int = 0, table: RopeTable | None = None, bq=None, bk=None,
+                    bv=None, q_out: torch.Tensor | None = None, stream=None):
+        _need_cuda(q, k, v, seq_ids, positions, bq, bk, bv, q_out)
+        n = seq_ids.numel()
+        check(load().hx_rope_append(self.handle, layer, _ptr(q), _ptr(k), _ptr(v), _dt(k), _ptr(bq),
+                                    _ptr(bk), _ptr(bv), _ptr(seq_ids), _ptr(positions), n,
+                                    num_q_heads, table.handle if table else None, _ptr(q_out),
+                                    _dt(q_out) if q_out is not None else HX_FP16,
+                                    _stream(stream)), "rope_append")
+
+    def workspace_bytes(self, n_seqs: int, num_q_heads: int) -> int:
+        return int(load().hx_decode_workspace_bytes(self.handle, n_seqs, num_q_heads))
+
+    def decode(self, layer: int, q: torch.Tensor, seq_ids: torch.Tensor, lengths: torch.Tensor,
+               num_q_heads: int, *, scale: float | None = None, out: torch.Tensor | None = None,
+               out_dtype=torch.float16, workspace: torch.Tensor | None = None, stream=None):
+        _need_cuda(q, seq_ids, lengths, out, workspace)
+        n = seq_ids.numel()
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            out = torch.empty((n, num_q_heads * self.head_dim), dtype=out_dtype, device=q.device)
+        ws_need = self.workspace_bytes(n, num_q_heads)
+        if workspace is None:
+            workspace = torch.empty(max(ws_need, 16), dtype=torch.uint8, device=q.device)
+        check(load().hx_decode_attention(self.handle, layer, _ptr(q), _dt(q), _ptr(seq_ids),
+                                         _ptr(lengths), n, num_q_heads, scale, _ptr(out), _dt(out),
+                                         _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                         _stream(stream)), "decode attention")
+        return out
+
+    def snapshot_bytes(self, prefix_len: int) -> int:
+        return int(load().hx_snapshot_bytes(self.handle, prefix_len))
+
+    def snapshot(self, seq: int, prefix_len: int, dst: torch.Tensor | None = None, stream=None):
+        nbytes = self.snapshot_bytes(prefix_len)
+        if dst is None:
+            dst = torch.empty(max(nbytes, 16), dtype=torch.uint8,
+                              device=torch.device("cuda", torch.cuda.current_device()))
+        _need_cuda(dst)
+        check(load().hx_kv_snapshot(self.handle, seq, prefix_len, _ptr(dst),
+                                    dst.numel() * dst.element_size(), _stream(stream)), "snapshot")
+        return dst
+
+    def restore(self, seq: int, prefix_len: int, src: torch.Tensor, stream=None):
+        _need_cuda(src)
+        check(load().hx_kv_restore(self.handle, seq, prefix_len, _ptr(src),
+                                   src.numel() * src.element_size(), _stream(stream)), "restore")

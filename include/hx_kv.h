@@ -1,0 +1,210 @@
+/*
+ * hx_kv.h — C ABI of the B200 (sm_100a) KV-cache hot path for hxinfer.
+ *
+ * The library (hxinfer_b200/libhxkv.so) replaces, behind hxinfer's own operator
+ * and layer interfaces, the reference engine's
+ *   - KV append + decode attention  hxinfer-engine/src/op/cuda/attention_score_cuda.cu:7-214
+ *                                   (declared hxinfer-engine/include/op/math_ops.h:67-73)
+ *   - RoPE                          hxinfer-engine/src/op/cuda/rope_cuda.cu:46-152,
+ *                                   hxinfer-engine/src/op/cpu/rope_cpu.cpp:5-39
+ *                                   (declared math_ops.h:28-30)
+ *   - QKV bias add                  hxinfer-engine/src/op/cuda/bias_add.cu:20-30
+ *   - the per-layer K/V cache       hxinfer-engine/include/layer/attention.h:49-51,82-84
+ *   - PrefixCacheManager copies     hxinfer-engine/include/cache/prefix_cache.h:58-151
+ *
+ * Conventions
+ *   - Every entry point returns an int status (HX_OK = 0, else HX_ERR_*); the
+ *     message of the last failure on the calling thread is in hx_last_error().
+ *     Nothing is printed.
+ *   - Every launch takes a CUDA stream and never synchronises it.  Kernel-side
+ *     faults (an out-of-range position, a missing cache block, a bounded wait
+ *     that ran out) are recorded in a per-device status word that
+ *     hx_device_status() reads back.
+ *   - Pointers marked "device" are CUDA device pointers; sizes are in elements
+ *     unless the name ends in _bytes.  No torch or C++ types cross this ABI.
+ *   - A cache handle is thread-compatible: one host thread at a time per
+ *     handle; concurrency comes from streams.
+ *
+ * KV layout in HBM (head-major, 128-byte aligned blocks)
+ *   One pool per cache: [layer][K|V][block][kv_head][64 tokens][head_dim] fp16.
+ *   A block holds 64 consecutive positions of one sequence; a per-sequence
+ *   block table maps logical block -> physical block.  Each (block, kv_head)
+ *   tile is a contiguous 64*head_dim*2-byte run (16 KiB at head_dim 128),
+ *   which is one TMA tile of the decode kernel.
+ */
+#ifndef HX_KV_H
+#define HX_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* hx_stream_t; /* same type as cudaStream_t */
+
+enum hx_status {
+    HX_OK = 0,
+    HX_ERR_INVALID = 1,     /* bad argument, shape or dtype */
+    HX_ERR_CAPACITY = 2,    /* position / length / pool capacity exceeded */
+    HX_ERR_OOM = 3,         /* device or host allocation failed */
+    HX_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+    HX_ERR_NCCL = 5,        /* a collective failed */
+    HX_ERR_TIMEOUT = 6,     /* a bounded device-side wait ran out */
+    HX_ERR_NOT_FOUND = 7,   /* unknown sequence or snapshot */
+    HX_ERR_UNSUPPORTED = 8  /* valid request this build does not implement */
+};
+
+/* Element types; the values are the reference's DataType codes
+ * (hxinfer-engine/include/base/config.h:5-10). */
+enum hx_dtype { HX_FP32 = 1, HX_FP16 = 3 };
+
+const char* hx_status_string(int status);
+/* Message of the last failed call on this thread ("" if none). */
+const char* hx_last_error(void);
+/* Reads (and, if clear != 0, resets) the device-side status word of the
+ * current device.  Synchronises the device.  Returns HX_OK or the first
+ * HX_ERR_* a kernel recorded since the last reset. */
+int hx_device_status(int clear);
+
+/* ------------------------------------------------------------ KV cache */
+
+typedef struct hx_kv_cache hx_kv_cache;
+
+typedef struct {
+    int32_t num_layers;
+    int32_t num_kv_heads;        /* heads held by this cache (a shard may hold a subset) */
+    int32_t head_dim;            /* even, <= 256; 128 takes the TMA decode path */
+    int32_t max_seqs;
+    int32_t max_tokens_per_seq;  /* per-sequence capacity in positions */
+    int64_t num_blocks;          /* physical 64-token blocks; 0 = max_seqs * ceil(max_tokens/64) */
+} hx_kv_config;
+
+typedef struct {
+    int32_t num_layers, num_kv_heads, head_dim, max_seqs, max_blocks_per_seq;
+    int64_t num_blocks, free_blocks;
+    void* pool;                  /* device; NULL for a wrapped cache */
+    size_t pool_bytes;
+    int64_t layer_stride_bytes, kv_stride_bytes, block_stride_bytes, head_stride_bytes;
+    int32_t* block_table;        /* device [max_seqs][max_blocks_per_seq], -1 = unmapped */
+} hx_kv_info;
+
+/* Allocates the pool and block table (replaces the per-layer cache tensors of
+ * AttentionLayer, attention.h:49-51). */
+int hx_kv_create(const hx_kv_config* cfg, hx_kv_cache** out);
+
+/* Wraps caller memory as a one-layer, one-sequence cache with the contiguous
+ * head-major layout [num_kv_heads][capacity][head_dim] fp16 for K and V.
+ * This is how the kept operator attention_score_cuda(q, k, v, k_cache,
+ * v_cache, out, config, pos) (math_ops.h:67-73) uses the caller's k_cache /
+ * v_cache tensors: storage stays opaque to the caller. */
+int hx_kv_wrap(void* k_base, void* v_base, int num_kv_heads, int head_dim, int capacity,
+               hx_kv_cache** out);
+
+int hx_kv_destroy(hx_kv_cache* cache);
+int hx_kv_get_info(const hx_kv_cache* cache, hx_kv_info* out);
+
+/* Makes sequence `seq` able to hold n_tokens positions, mapping blocks from
+ * the pool's free list; the block-table row is updated on `stream`. */
+int hx_kv_reserve(hx_kv_cache* cache, int seq, int n_tokens, hx_stream_t stream);
+/* Returns every block of `seq` to the free list. */
+int hx_kv_release(hx_kv_cache* cache, int seq, hx_stream_t stream);
+
+/* Copies n token rows (token-major [n][num_kv_heads*head_dim], dtype
+ * HX_FP16 or HX_FP32, device) into positions [start, start+n) of (layer, seq)
+ * without rotation; fp32 input is rounded to fp16 (RNE). */
+int hx_kv_write(hx_kv_cache* cache, int layer, int seq, int start, int n, const void* k,
+                const void* v, int dtype, hx_stream_t stream);
+/* Gathers positions [start, start+n) of (layer, seq) into token-major fp16
+ * rows [n][num_kv_heads*head_dim] (device); k or v may be NULL. */
+int hx_kv_read(const hx_kv_cache* cache, int layer, int seq, int start, int n, void* k, void* v,
+               hx_stream_t stream);
+/* Fills every block of the pool with N(0,1) values rounded to fp16, from a
+ * counter-based generator keyed by `seed` (synthetic benchmark caches). */
+int hx_kv_fill_normal(hx_kv_cache* cache, uint64_t seed, hx_stream_t stream);
+
+/* ------------------------------------------------------------ RoPE */
+
+typedef struct hx_rope_table hx_rope_table;
+
+typedef struct {
+    int32_t head_dim;
+    int32_t max_pos;            /* positions [0, max_pos) */
+    float theta;                /* base; ModelConfig::rope_theta (config.h:41) */
+    int32_t use_yarn;           /* ModelConfig::rope_use_yarn (config.h:43) */
+    float yarn_factor, yarn_beta_fast, yarn_beta_slow;
+    int32_t yarn_orig_max_pos;
+} hx_rope_config;
+
+/* Builds the device cos/sin table [max_pos][head_dim/2] holding exactly the
+ * cos/sin values rope_cpu computes (rope_cpu.cpp:22-25), or with use_yarn the
+ * YaRN-scaled values of rope_cuda (rope_cuda.cu:56-61, 112-121). */
+int hx_rope_table_create(const hx_rope_config* cfg, hx_rope_table** out);
+int hx_rope_table_destroy(hx_rope_table* table);
+
+/* In-place NeoX RoPE of q [rows][num_q_heads*head_dim] and k
+ * [rows][num_kv_heads*head_dim] (device, HX_FP16 or HX_FP32) at one position
+ * `step`.  Replaces rope_cuda (rope_cuda.cu:98-152); the result equals
+ * rope_cpu (rope_cpu.cpp:5-39) bit for bit. */
+int hx_rope_qk(void* q, void* k, int dtype, int rows, int num_q_heads, int num_kv_heads,
+               int head_dim, int step, const hx_rope_table* table, hx_stream_t stream);
+
+/* K1: fused QKV bias + RoPE + K/V append.  For each token i:
+ *   q' = rope(q[i] + bq), k' = rope(k[i] + bk), v' = v[i] + bv,
+ *   cache(layer, seq_ids[i], positions[i]) <- (k', v') in fp16,
+ *   q_out[i] <- q' in q_out_dtype.
+ * q/k/v rows as in the reference ([n][Hq*hd], [n][Hkv*hd]) in `dtype`;
+ * biases (same dtype) may be NULL; table may be NULL (no rotation: a plain
+ * append, as attention_score_cuda.cu:7-15 does); q/q_out may be NULL.
+ * The fp16 bias add rounds like bias_add.cu:6-11 (__hadd).
+ * seq_ids/positions: device int32 [n_tokens]. */
+int hx_rope_append(hx_kv_cache* cache, int layer, const void* q, const void* k, const void* v,
+                   int dtype, const void* bq, const void* bk, const void* bv,
+                   const int32_t* seq_ids, const int32_t* positions, int n_tokens,
+                   int num_q_heads, const hx_rope_table* table, void* q_out, int q_out_dtype,
+                   hx_stream_t stream);
+
+/* ------------------------------------------------------------ attention */
+
+/* Workspace bytes hx_decode_attention needs for n_seqs sequences
+ * (split-K partial results; device memory owned by the caller). */
+size_t hx_decode_workspace_bytes(const hx_kv_cache* cache, int n_seqs, int num_q_heads);
+
+/* K2: split-K GQA decode attention over the cache (replaces
+ * attention_score_kernel, attention_score_cuda.cu:17-83,95-161).
+ * q: device [n_seqs][num_q_heads*head_dim] (rotated) in q_dtype;
+ * seq_ids, lengths: device int32 [n_seqs] (lengths = positions attended, >= 1);
+ * out: device [n_seqs][num_q_heads*head_dim] in out_dtype.
+ * q head h reads kv head h / (num_q_heads / num_kv_heads). */
+int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
+                        const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                        int num_q_heads, float scale, void* out, int out_dtype, void* workspace,
+                        size_t workspace_bytes, hx_stream_t stream);
+
+/* ------------------------------------------------------------ prefix snapshots */
+
+/* Bytes of a snapshot of the first prefix_len positions of one sequence:
+ * layers * 2 * num_kv_heads * prefix_len * head_dim * 2. */
+size_t hx_snapshot_bytes(const hx_kv_cache* cache, int prefix_len);
+
+/* K4: copies positions [0, prefix_len) of every layer's K and V of `seq` into
+ * dst (device, layout [layer][K|V][kv_head][prefix_len][head_dim] fp16).
+ * Replaces the host memcpy of PrefixCacheManager::store (prefix_cache.h:78-89). */
+int hx_kv_snapshot(const hx_kv_cache* cache, int seq, int prefix_len, void* dst,
+                   size_t dst_bytes, hx_stream_t stream);
+/* Copies a snapshot back into positions [0, prefix_len) of `seq` (which must
+ * be reserved for prefix_len positions); later positions are untouched.
+ * Replaces PrefixCacheManager::restore's memcpy (prefix_cache.h:135-147). */
+int hx_kv_restore(hx_kv_cache* cache, int seq, int prefix_len, const void* src,
+                  size_t src_bytes, hx_stream_t stream);
+
+/* FNV-1a 64 of the token ids (PrefixCacheManager::compute_hash,
+ * prefix_cache.h:42-49); host function. */
+uint64_t hx_prefix_hash(const int32_t* tokens, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HX_KV_H */

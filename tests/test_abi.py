@@ -1,0 +1,60 @@
+"""libhxkv.so loads without a GPU and exports every function include/*.h
+declares; host-only entry points behave without touching a device."""
+import glob
+import os
+import re
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for hdr in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(hdr).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        for m in re.finditer(r"\b(hx_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_exports_every_declared_symbol(hxlib):
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in sorted(names) if not hasattr(hxlib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_python_binding_covers_the_header():
+    from hxinfer_b200 import _lib
+    assert declared_functions() <= set(_lib.SIGNATURES), \
+        sorted(declared_functions() - set(_lib.SIGNATURES))
+
+
+def test_prefix_hash_matches_oracle(hxlib, oracle):
+    from hxinfer_b200 import kv
+    rng = np.random.default_rng(11)
+    for n in (0, 1, 5, 2048):
+        toks = rng.integers(-3, 152064, n).astype(np.int32)
+        assert kv.prefix_hash(toks.tolist()) == oracle.fnv1a64(toks)
+
+
+def test_status_strings(hxlib):
+    assert hxlib.hx_status_string(0) == b"ok"
+    assert hxlib.hx_status_string(2) == b"capacity exceeded"
+    assert hxlib.hx_status_string(999) == b"unknown status"
+
+
+def test_null_arguments_are_rejected_without_a_device(hxlib):
+    import ctypes as C
+    from hxinfer_b200 import _lib
+    out = C.c_void_p()
+    assert hxlib.hx_kv_create(None, C.byref(out)) == _lib.HX_ERR_INVALID
+    assert b"null config" in hxlib.hx_last_error()
+    bad = _lib.hx_kv_config(num_layers=1, num_kv_heads=1, head_dim=127, max_seqs=1,
+                            max_tokens_per_seq=8, num_blocks=0)
+    assert hxlib.hx_kv_create(C.byref(bad), C.byref(out)) == _lib.HX_ERR_INVALID
+    assert hxlib.hx_decode_workspace_bytes(None, 1, 1) == 0
+    assert hxlib.hx_snapshot_bytes(None, 4) == 0

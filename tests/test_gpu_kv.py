@@ -1,0 +1,338 @@
+"""GPU parity of the KV-cache hot path against the CPU oracle.
+
+Bars (stated where they are checked):
+  * RoPE, append, snapshot and restore: bit-exact against the oracle
+    (the oracle is pinned to the reference's own CPU ops).
+  * Attention: |gpu - oracle| <= 2e-3 + 1e-2 * |oracle| elementwise
+    (max-abs 2e-3 / max-rel 1e-2 of the fp32 CPU result).
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+@pytest.fixture(scope="module")
+def hx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hxinfer_b200 import kv
+    kv.load()
+    kv.device_status(clear=True)
+    return kv
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def h16(rng, shape, scale=1.0):
+    return (rng.standard_normal(shape) * scale).astype(np.float16)
+
+
+def u16(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy()
+
+
+def assert_close(got, want, what=""):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = np.abs(got - want)
+    bad = err > ATOL + RTOL * np.abs(want)
+    assert not bad.any(), (f"{what}: {bad.sum()} of {bad.size} outside tolerance; "
+                           f"max abs err {err.max():.3e}")
+
+
+def make_cache(hx, layers, hkv, max_seqs, cap, hd=128):
+    return hx.KVCache(layers, hkv, hd, max_seqs, cap)
+
+
+# ------------------------------------------------------------------ K1
+
+@pytest.mark.parametrize("in_dtype", [np.float16, np.float32])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_rope_append_bit_exact(hx, oracle, in_dtype, with_bias):
+    """Qwen2.5-7B shape (28 q / 4 kv heads), theta 1e6: rotated q, rotated K
+    and V in the cache equal the oracle (rope_cpu + fp16 rounding) bit for bit."""
+    rng = np.random.default_rng(10 + with_bias)
+    Hq, Hkv, hd, theta = 28, 4, 128, 1e6
+    positions = np.array([0, 1, 63, 64, 127, 1024, 4095], np.int32)
+    seqs = np.array([0, 1, 2, 0, 1, 2, 3], np.int32)
+    n = len(positions)
+    q = h16(rng, (n, Hq * hd)).astype(in_dtype)
+    k = h16(rng, (n, Hkv * hd)).astype(in_dtype)
+    v = h16(rng, (n, Hkv * hd)).astype(in_dtype)
+    bq = h16(rng, Hq * hd, 0.02).astype(in_dtype) if with_bias else None
+    bk = h16(rng, Hkv * hd, 0.02).astype(in_dtype) if with_bias else None
+    bv = h16(rng, Hkv * hd, 0.02).astype(in_dtype) if with_bias else None
+    cache = make_cache(hx, 2, Hkv, 4, 4096)
+    for s in range(4):
+        cache.reserve(s, 4096)
+    table = hx.RopeTable(hd, 4096, theta)
+    tdt = torch.float16 if in_dtype == np.float16 else torch.float32
+    q_out = torch.empty((n, Hq * hd), dtype=tdt, device="cuda")
+    cache.rope_append(1, dev(k), dev(v), dev(seqs), dev(positions), q=dev(q), num_q_heads=Hq,
+                      table=table, bq=None if bq is None else dev(bq),
+                      bk=None if bk is None else dev(bk), bv=None if bv is None else dev(bv),
+                      q_out=q_out)
+    torch.cuda.synchronize()
+    hx.device_status()
+
+    def biased(x, b):
+        if b is None:
+            return x.astype(np.float32)
+        if in_dtype == np.float16:  # __hadd: correctly rounded fp16 sum
+            return (x + b).astype(np.float16).astype(np.float32)
+        return (x.astype(np.float32) + b.astype(np.float32)).astype(np.float32)
+
+    for i in range(n):
+        wq = oracle.rope(biased(q[i], bq)[None], Hq, hd, int(positions[i]), theta)[0]
+        wk = oracle.rope(biased(k[i], bk)[None], Hkv, hd, int(positions[i]), theta)[0]
+        wv = biased(v[i], bv)
+        gq = q_out[i].cpu().numpy()
+        if in_dtype == np.float16:
+            assert np.array_equal(gq.view(np.int16), wq.astype(np.float16).view(np.int16))
+        else:
+            assert np.array_equal(gq.view(np.uint32), wq.view(np.uint32))
+        ck, cv = cache.read(1, int(seqs[i]), int(positions[i]), 1)
+        assert np.array_equal(u16(ck).reshape(-1), wk.astype(np.float16).view(np.int16))
+        assert np.array_equal(u16(cv).reshape(-1), wv.astype(np.float16).view(np.int16))
+
+
+def test_rope_qk_reference_kat(hx):
+    """rope_tensor KAT (tests/unit/test_unit_ops.cpp:197-229) through hx_rope_qk, fp32."""
+    table = hx.RopeTable(4, 8, 10000.0)
+    for step, want in ((0, [1.0, 2.0, 3.0, 4.0]), (1, [-1.9841, None, 2.4624, None])):
+        q = torch.tensor([[1.0, 2.0, 3.0, 4.0]], device="cuda")
+        k = q.clone()
+        hx.rope_qk(q, k, 1, 1, 4, step, table)
+        got = q.cpu().numpy()[0]
+        for g, w in zip(got, want):
+            if w is not None:
+                assert abs(g - w) < (1e-5 if step == 0 else 1e-3)
+
+
+def test_rope_qk_bit_exact_fp32(hx, oracle):
+    rng = np.random.default_rng(12)
+    Hq, Hkv, hd = 32, 8, 128
+    table = hx.RopeTable(hd, 33000, 5e5)
+    for step in (0, 17, 32768):
+        q = rng.standard_normal((3, Hq * hd)).astype(np.float32)
+        k = rng.standard_normal((3, Hkv * hd)).astype(np.float32)
+        tq, tk = dev(q), dev(k)
+        hx.rope_qk(tq, tk, Hq, Hkv, hd, step, table)
+        assert np.array_equal(tq.cpu().numpy().view(np.uint32),
+                              oracle.rope(q, Hq, hd, step, 5e5).view(np.uint32))
+        assert np.array_equal(tk.cpu().numpy().view(np.uint32),
+                              oracle.rope(k, Hkv, hd, step, 5e5).view(np.uint32))
+
+
+def test_append_out_of_capacity_is_recorded_not_written(hx):
+    cache = make_cache(hx, 1, 2, 2, 128)
+    cache.reserve(0, 64)  # only the first block is mapped
+    k = torch.ones((1, 256), dtype=torch.float16, device="cuda")
+    cache.rope_append(0, k, k, dev(np.array([0], np.int32)), dev(np.array([100], np.int32)))
+    torch.cuda.synchronize()
+    from hxinfer_b200._lib import HXError, HX_ERR_CAPACITY
+    with pytest.raises(HXError) as e:
+        hx.device_status(clear=True)
+    assert e.value.status == HX_ERR_CAPACITY
+    hx.device_status(clear=True)  # cleared
+
+
+# ------------------------------------------------------------------ K2
+
+def oracle_decode_case(oracle, rng, Hq, Hkv, lengths, theta=1e6, hd=128):
+    """Caches of N(0,1) fp16 rows, a new token per sequence rotated at
+    position L-1; returns inputs and the oracle outputs."""
+    cases = []
+    for L in lengths:
+        kc = oracle.f16(rng.standard_normal((L, Hkv * hd)))
+        vc = oracle.f16(rng.standard_normal((L, Hkv * hd)))
+        q = oracle.f16(rng.standard_normal(Hq * hd))
+        cases.append((kc, vc, q))
+    return cases
+
+
+def run_decode(hx, oracle, Hq, Hkv, lengths, hd=128, out_dtype=torch.float16, seed=0,
+               q_dtype=torch.float16):
+    rng = np.random.default_rng(seed)
+    cases = oracle_decode_case(oracle, rng, Hq, Hkv, lengths, hd=hd)
+    cap = max(lengths)
+    cache = make_cache(hx, 2, Hkv, len(lengths) + 1, cap, hd)
+    # sequence ids deliberately not equal to the batch index
+    seq_ids = np.array([(i + 1) % (len(lengths) + 1) for i in range(len(lengths))], np.int32)
+    for i, (kc, vc, q) in enumerate(cases):
+        cache.reserve(int(seq_ids[i]), lengths[i])
+        cache.write(1, int(seq_ids[i]), 0, dev(kc, torch.float16), dev(vc, torch.float16))
+    qs = dev(np.stack([c[2] for c in cases]), q_dtype)
+    out = cache.decode(1, qs, dev(seq_ids), dev(np.array(lengths, np.int32)), Hq,
+                       scale=1.0 / math.sqrt(hd), out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    hx.device_status()
+    got = out.float().cpu().numpy()
+    for i, (kc, vc, q) in enumerate(cases):
+        want = oracle.decode_attention(q, kc, vc, Hq, Hkv, hd)
+        assert_close(got[i], want, f"seq {i} L={lengths[i]} Hq={Hq} Hkv={Hkv} hd={hd}")
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (32, 8), (32, 32), (32, 2), (4, 4)])
+def test_decode_gqa_groups(hx, oracle, Hq, Hkv):
+    run_decode(hx, oracle, Hq, Hkv, [1025], seed=Hq + Hkv)
+
+
+@pytest.mark.parametrize("lengths", [[1], [2], [63], [64], [65], [127, 128, 129], [1, 5000, 64, 3]])
+def test_decode_ragged_lengths(hx, oracle, lengths):
+    run_decode(hx, oracle, 28, 4, lengths, seed=sum(lengths))
+
+
+def test_decode_fp32_in_out(hx, oracle):
+    run_decode(hx, oracle, 32, 8, [300, 77], out_dtype=torch.float32, q_dtype=torch.float32, seed=3)
+
+
+def test_decode_qwen_32k(hx, oracle):
+    """The north-star shape: Qwen2.5-7B GQA 28/4, 32,769 positions."""
+    run_decode(hx, oracle, 28, 4, [32769], seed=32)
+
+
+def test_decode_batched_llama3(hx, oracle):
+    """LLaMA-3-8B shape, 16 sequences of ragged lengths in [512, 8192]."""
+    lengths = list(np.random.default_rng(44).integers(512, 8193, 16))
+    run_decode(hx, oracle, 32, 8, [int(x) for x in lengths], seed=44)
+
+
+@pytest.mark.parametrize("hd", [64, 2])
+def test_decode_generic_head_dim(hx, oracle, hd):
+    run_decode(hx, oracle, 4, 2, [1, 70, 200], hd=hd, seed=hd)
+
+
+def test_fused_decode_step_qwen_c1(hx, oracle):
+    """Config 1: Qwen2.5-7B layer, cache of 1024 N(0,1) tokens, one new token
+    (q/k/v ~ N(0,1)) rotated at position 1024 (theta 1e6), appended, then
+    softmax(QK^T/sqrt(128))V over 1025 positions."""
+    rng = np.random.default_rng(1)
+    Hq, Hkv, hd, theta, P = 28, 4, 128, 1e6, 1024
+    kc = oracle.f16(rng.standard_normal((P, Hkv * hd)))
+    vc = oracle.f16(rng.standard_normal((P, Hkv * hd)))
+    q = h16(rng, (1, Hq * hd))
+    k = h16(rng, (1, Hkv * hd))
+    v = h16(rng, (1, Hkv * hd))
+    cache = make_cache(hx, 1, Hkv, 1, 2048)
+    cache.reserve(0, P + 1)
+    cache.write(0, 0, 0, dev(kc, torch.float16), dev(vc, torch.float16))
+    table = hx.RopeTable(hd, 2048, theta)
+    q_out = torch.empty((1, Hq * hd), dtype=torch.float16, device="cuda")
+    sid = dev(np.array([0], np.int32))
+    cache.rope_append(0, dev(k), dev(v), sid, dev(np.array([P], np.int32)), q=dev(q),
+                      num_q_heads=Hq, table=table, q_out=q_out)
+    out = cache.decode(0, q_out, sid, dev(np.array([P + 1], np.int32)), Hq)
+    torch.cuda.synchronize()
+    hx.device_status()
+    qr = oracle.rope(q.astype(np.float32), Hq, hd, P, theta)
+    kr = oracle.rope(k.astype(np.float32), Hkv, hd, P, theta)
+    K = np.concatenate([kc, oracle.f16(kr)])
+    V = np.concatenate([vc, v.astype(np.float32)])
+    want = oracle.decode_attention(qr[0], K, V, Hq, Hkv, hd)
+    assert_close(out.float().cpu().numpy()[0], want, "config-1 step")
+
+
+def test_wrapped_cache_reference_kat(hx):
+    """attention_score_cuda KAT (tests/unit/test_unit_ops.cpp:292-319) through a
+    wrapped caller cache: one head, head_dim 2, pos 0 -> out = V = [5, 10]."""
+    kbuf = torch.full((10, 2), float("nan"), dtype=torch.float32, device="cuda")
+    vbuf = torch.full((10, 2), float("nan"), dtype=torch.float32, device="cuda")
+    cache = hx.KVCache.wrap(kbuf, vbuf, 1, 2, 10)
+    sid, pos = dev(np.array([0], np.int32)), dev(np.array([0], np.int32))
+    k = torch.tensor([[1.0, 0.0]], device="cuda")
+    v = torch.tensor([[5.0, 10.0]], device="cuda")
+    cache.rope_append(0, k, v, sid, pos)
+    q = torch.tensor([[1.0, 0.0]], device="cuda")
+    out = cache.decode(0, q, sid, dev(np.array([1], np.int32)), 1, scale=1 / math.sqrt(2),
+                       out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    hx.device_status()
+    r = out.cpu().numpy()[0]
+    assert abs(r[0] - 5.0) < 1e-3 and abs(r[1] - 10.0) < 1e-3
+
+
+def test_wrapped_cache_tma_path(hx, oracle):
+    """A wrapped head-major cache whose capacity is not a multiple of 64, read
+    through the TMA path, with NaN garbage past the sequence end."""
+    rng = np.random.default_rng(21)
+    Hq, Hkv, hd, cap, L = 8, 2, 128, 100, 90
+    kbuf = torch.full((Hkv * cap * hd,), float("nan"), dtype=torch.float16, device="cuda")
+    vbuf = torch.full_like(kbuf, float("nan"))
+    cache = hx.KVCache.wrap(kbuf, vbuf, Hkv, hd, cap)
+    kc = oracle.f16(rng.standard_normal((L, Hkv * hd)))
+    vc = oracle.f16(rng.standard_normal((L, Hkv * hd)))
+    cache.write(0, 0, 0, dev(kc, torch.float16), dev(vc, torch.float16))
+    q = oracle.f16(rng.standard_normal(Hq * hd))
+    out = cache.decode(0, dev(q[None], torch.float16), dev(np.array([0], np.int32)),
+                       dev(np.array([L], np.int32)), Hq)
+    torch.cuda.synchronize()
+    hx.device_status()
+    assert_close(out.float().cpu().numpy()[0], oracle.decode_attention(q, kc, vc, Hq, Hkv, hd))
+
+
+# ------------------------------------------------------------------ K4
+
+def test_snapshot_restore_bit_exact(hx):
+    """PrefixCacheManager semantics (prefix_cache.h:58-151) on the device: the
+    snapshot holds the first prefix_len positions of every layer's K and V;
+    restore puts them back and leaves later positions untouched."""
+    layers, Hkv, hd, plen, total = 4, 4, 128, 200, 300
+    cache = make_cache(hx, layers, Hkv, 3, 512)
+    cache.reserve(0, total)
+    cache.reserve(2, total)
+    cache.fill_normal(1234)
+    before = [cache.read(l, 0, 0, total) for l in range(layers)]
+    snap = cache.snapshot(0, plen)
+    torch.cuda.synchronize()
+    # layout [layer][K|V][kv_head][prefix_len][head_dim]
+    s = snap.view(torch.float16).view(layers, 2, Hkv, plen, hd)
+    for l in range(layers):
+        for kv in range(2):
+            want = before[l][kv][:plen].permute(1, 0, 2)
+            assert torch.equal(s[l, kv].view(torch.int16), want.contiguous().view(torch.int16))
+    # overwrite seq 2 with other values, restore seq 0's prefix into it
+    other = [cache.read(l, 2, 0, total) for l in range(layers)]
+    cache.restore(2, plen, snap)
+    torch.cuda.synchronize()
+    hx.device_status()
+    for l in range(layers):
+        k2, v2 = cache.read(l, 2, 0, total)
+        assert torch.equal(k2[:plen].view(torch.int16), before[l][0][:plen].view(torch.int16))
+        assert torch.equal(v2[:plen].view(torch.int16), before[l][1][:plen].view(torch.int16))
+        assert torch.equal(k2[plen:].view(torch.int16), other[l][0][plen:].view(torch.int16))
+        assert torch.equal(v2[plen:].view(torch.int16), other[l][1][plen:].view(torch.int16))
+
+
+def test_snapshot_rejects_unreserved_prefix(hx):
+    cache = make_cache(hx, 1, 1, 1, 256)
+    cache.reserve(0, 64)
+    from hxinfer_b200._lib import HXError
+    with pytest.raises(HXError):
+        cache.snapshot(0, 65)
+
+
+def test_block_allocator_release_and_reuse(hx):
+    cache = make_cache(hx, 1, 2, 2, 256)
+    info = cache.info()
+    assert info["free_blocks"] == 8
+    cache.reserve(0, 256)
+    cache.reserve(1, 65)
+    assert cache.info()["free_blocks"] == 2
+    cache.release(0)
+    assert cache.info()["free_blocks"] == 6
+    from hxinfer_b200._lib import HXError
+    with pytest.raises(HXError):
+        cache.reserve(1, 257)
