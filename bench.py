@@ -59,11 +59,13 @@ def peaks():
 # ------------------------------------------------------------------ partitioning
 
 def partition(world: int, rank: int, lengths):
-    """(mode, seq indices, kv-head indices) this rank holds."""
+    """(mode, seq indices, kv-head indices, padded rows) for this rank; every
+    rank's output block is padded to the largest shard's row count so the
+    all-gather is uniform."""
     from hxinfer_b200.dist import plan
     mode, shards = plan(world, HKV, lengths)
     seqs, heads = shards[rank]
-    return mode, seqs, heads
+    return mode, seqs, heads, max(len(s) for s, _ in shards)
 
 
 # ------------------------------------------------------------------ clocks
@@ -197,7 +199,7 @@ def run_batched_decode(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     lengths = lengths_c4()
-    mode, seqs, heads = partition(world, rank, lengths)
+    mode, seqs, heads, n_pad = partition(world, rank, lengths)
     hkv = len(heads)
     hq = hkv * (HQ // HKV)
     n = len(seqs)
@@ -218,8 +220,8 @@ def run_batched_decode(args):
     k_in = torch.randn((LAYERS, n, hkv * HD), generator=g, device=dev).half()
     v_in = torch.randn((LAYERS, n, hkv * HD), generator=g, device=dev).half()
     q_rot = torch.empty_like(q_in)
-    out = torch.empty((LAYERS, n, hq * HD), dtype=torch.float16, device=dev)
-    gathered = torch.empty((LAYERS, world, n, hq * HD), dtype=torch.float16, device=dev) \
+    out = torch.zeros((LAYERS, n_pad, hq * HD), dtype=torch.float16, device=dev)
+    gathered = torch.empty((LAYERS, world, n_pad, hq * HD), dtype=torch.float16, device=dev) \
         if world > 1 else None
     seq_ids = torch.arange(n, dtype=torch.int32, device=dev)
     total_steps = W + 2 * K
@@ -378,7 +380,7 @@ def run_batched_decode(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="batched_decode",

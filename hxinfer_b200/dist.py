@@ -20,15 +20,15 @@ import numpy as np
 
 
 def balance_sequences(lengths, world: int):
-    """Greedy longest-first assignment of sequences to `world` groups so the
-    total cached length per group is balanced; each group sorted."""
+    """Deal sequences, longest first, to `world` groups in snake order
+    (0..W-1, W-1..0, ...): group sizes differ by at most one (so an all-gather
+    of padded per-rank outputs stays uniform) and total lengths stay close.
+    Each group is returned sorted."""
     order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
-    load = [0] * world
     groups = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda j: (load[j], j))
-        groups[r].append(i)
-        load[r] += int(lengths[i])
+    for k, i in enumerate(order):
+        rnd, pos = divmod(k, world)
+        groups[pos if rnd % 2 == 0 else world - 1 - pos].append(i)
     return [sorted(g) for g in groups]
 
 
