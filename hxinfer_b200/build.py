@@ -21,6 +21,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libhxkv.so")
+CPP = os.path.join(PKG, "cpp")
+CPPLIB = os.path.join(PKG, "libhxinfer.so")
+CUDA_LIB = "/usr/local/cuda/lib64"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
@@ -72,6 +75,47 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     return LIB
 
 
+def build_cpp(verbose: bool = False) -> str:
+    """libhxinfer.so: the C++ interface layer (Tensor, allocators, rope_tensor /
+    rope_cuda / attention_score_cuda, AttentionLayer, PrefixCacheManager) over
+    libhxkv.so; cuBLAS for the attention projections."""
+    build(verbose)
+    os.makedirs(OBJ, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CPP, "src", "*.cpp")) + glob.glob(os.path.join(CPP, "src", "*.cu")))
+    headers = glob.glob(os.path.join(CPP, "include", "*", "*.h")) + \
+        glob.glob(os.path.join(CPP, "src", "*.h")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    inc = [f"-I{os.path.join(CPP, 'include')}", f"-I{os.path.join(CPP, 'src')}",
+           f"-I{os.path.join(ROOT, 'include')}"]
+    objs = []
+    for src in srcs:
+        obj = os.path.join(OBJ, "cpp_" + os.path.basename(src) + ".o")
+        objs.append(obj)
+        if not _newer([src] + headers, obj):
+            continue
+        cmd = [nvcc()] + ARCH + ["-std=c++17", "-O2", "-lineinfo", "-Xcompiler", "-fPIC"] + inc + \
+            ["-x", "cu" if src.endswith(".cu") else "c++", "-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0 or verbose:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src}")
+    if _newer(objs + [LIB], CPPLIB):
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", CPPLIB] + objs + \
+            [f"-L{PKG}", "-lhxkv", f"-L{CUDA_LIB}", "-lcublas", "-Xlinker", "-rpath,$ORIGIN",
+             "-Xlinker", f"-rpath,{CUDA_LIB}"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("link of libhxinfer.so failed")
+    return CPPLIB
+
+
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv)
+    build_cpp(verbose="-v" in sys.argv)
     print(LIB)
+    print(CPPLIB)

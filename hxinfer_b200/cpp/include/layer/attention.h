@@ -1,0 +1,65 @@
+// layer/attention.h — AttentionLayer with the reference's constructors,
+// forward(input, output, pos) and cache getters
+// (hxinfer-engine/include/layer/attention.h:35-102).
+//
+// forward on CUDA tensors: q/k/v projections (cuBLAS GEMV, as the reference),
+// then ONE fused launch for the optional QKV bias + RoPE at `pos` + K/V append
+// (hx_rope_append), then split-K decode attention over pos+1 positions
+// (hx_decode_attention), then the o projection.  The per-layer cache lives in
+// k_cache_ / v_cache_ ([seq_len, kv_dim] fp16 tensors, head-major inside) and
+// is reached by PrefixCacheManager through get_k_cache()/get_v_cache() and
+// kv_cache().
+#ifndef HXINFER_B200_ATTENTION_H
+#define HXINFER_B200_ATTENTION_H
+#include <memory>
+#include <stdexcept>
+
+#include "base/allocator.h"
+#include "base/config.h"
+#include "hx_kv.h"
+#include "layer/layer.h"
+#include "tensor/tensor.h"
+
+namespace hxinfer {
+
+class AttentionLayer : public Layer {
+public:
+    AttentionLayer(std::shared_ptr<Allocator> allocator, ModelConfig& config,
+                   std::shared_ptr<Tensor>& wq, std::shared_ptr<Tensor>& wk,
+                   std::shared_ptr<Tensor>& wv, std::shared_ptr<Tensor>& wo);
+    AttentionLayer(std::shared_ptr<Allocator> allocator, ModelConfig& config,
+                   std::shared_ptr<Tensor>& wq, std::shared_ptr<Tensor>& wk,
+                   std::shared_ptr<Tensor>& wv, std::shared_ptr<Tensor>& wo,
+                   std::shared_ptr<Tensor>& bq, std::shared_ptr<Tensor>& bk,
+                   std::shared_ptr<Tensor>& bv);
+    ~AttentionLayer() override;
+
+    void forward(std::shared_ptr<Tensor>& input, std::shared_ptr<Tensor>& output, int pos);
+    void forward(std::shared_ptr<Tensor>&, std::shared_ptr<Tensor>&) override
+    {
+        throw std::runtime_error("AttentionLayer requires 'pos' parameter!\n");
+    }
+
+    std::shared_ptr<Tensor>& get_k_cache() { return k_cache_; }
+    std::shared_ptr<Tensor>& get_v_cache() { return v_cache_; }
+    // The cache handle over k_cache_/v_cache_ (for snapshots).
+    hx_kv_cache* kv_cache() const { return kv_; }
+
+private:
+    void init(std::shared_ptr<Allocator> allocator);
+    void project(const std::shared_ptr<Tensor>& w, const std::shared_ptr<Tensor>& x,
+                 std::shared_ptr<Tensor>& y);
+
+    ModelConfig config_;
+    std::shared_ptr<Tensor> wq_, wk_, wv_, wo_;
+    bool has_bias_ = false;
+    std::shared_ptr<Tensor> bq_, bk_, bv_;
+    std::shared_ptr<Tensor> curr_q_, curr_k_, curr_v_, q_rot_, x16_;
+    std::shared_ptr<Tensor> k_cache_, v_cache_;
+    std::shared_ptr<Tensor> after_qktv_;
+    DataType activation_dtype_;
+    hx_kv_cache* kv_ = nullptr;
+};
+
+}  // namespace hxinfer
+#endif

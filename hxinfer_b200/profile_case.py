@@ -1,0 +1,109 @@
+"""Small, self-contained cases of the hot-path kernels, sized for profiling.
+
+    python -m hxinfer_b200.profile_case decode  --shape llama3 --seqs 16 --len 8192 --layers 1 --iters 5
+    python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
+    python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
+
+Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
+prints one JSON line with the CUDA-event time per iteration and the
+algorithmic bytes, so the same command serves a timing check and an ncu
+capture (keep the device footprint to a few GB: inputs larger than the
+126 MB L2, small enough for ncu's memory save/restore between passes).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import kv
+
+SHAPES = {"llama3": (32, 8, 5e5), "qwen": (28, 4, 1e6), "llama2": (32, 32, 1e4)}
+
+
+def decode_case(a):
+    hq, hkv, theta = SHAPES[a.shape]
+    hd, n, L, layers = 128, a.seqs, a.len, a.layers
+    cap = L + a.iters + 2
+    cache = kv.KVCache(layers, hkv, hd, n, cap)
+    for s in range(n):
+        cache.reserve(s, cap)
+    cache.fill_normal(7)
+    table = kv.RopeTable(hd, cap, theta)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    q = torch.randn((layers, n, hq * hd), generator=g, device="cuda").half()
+    k = torch.randn((layers, n, hkv * hd), generator=g, device="cuda").half()
+    v = torch.randn((layers, n, hkv * hd), generator=g, device="cuda").half()
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
+    ws = torch.empty(cache.workspace_bytes(n, hq), dtype=torch.uint8, device="cuda")
+    evs = []
+    for it in range(a.iters):
+        pos = torch.full((n,), L - 1 + it, dtype=torch.int32, device="cuda")
+        lens = pos + 1
+        for l in range(layers):
+            cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
+                              q_out=q_rot[l])
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            cache.decode(l, q_rot[l], sid, lens, hq, out=out[l], workspace=ws)
+            e1.record()
+            evs.append((e0, e1))
+    torch.cuda.synchronize()
+    kv.device_status()
+    skip = min(len(evs) - 1, layers)  # first iteration is warm-up
+    ms = [x.elapsed_time(y) for x, y in evs[skip:]]
+    avg = sum(ms) / len(ms)
+    nbytes = 2 * n * (L + a.iters // 2) * hkv * hd * 2
+    print(json.dumps({"case": "decode", "shape": a.shape, "seqs": n, "len": L, "layers": layers,
+                      "decode_ms_avg": avg, "bytes_per_launch": nbytes,
+                      "gbs": nbytes / (avg * 1e-3) / 1e9}))
+
+
+def snapshot_case(a):
+    hq, hkv, _ = SHAPES[a.shape]
+    hd, L, layers = 128, a.len, a.layers
+    cache = kv.KVCache(layers, hkv, hd, 2, L)
+    cache.reserve(0, L)
+    cache.reserve(1, L)
+    cache.fill_normal(3)
+    snap = torch.empty(cache.snapshot_bytes(L), dtype=torch.uint8, device="cuda")
+    ts, tr = [], []
+    for _ in range(a.iters):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        cache.snapshot(0, L, snap)
+        e[1].record()
+        cache.restore(1, L, snap)
+        e[2].record()
+        ts.append(e)
+    torch.cuda.synchronize()
+    kv.device_status()
+    snap_ms = sum(x[0].elapsed_time(x[1]) for x in ts[1:]) / max(1, len(ts) - 1)
+    rest_ms = sum(x[1].elapsed_time(x[2]) for x in ts[1:]) / max(1, len(ts) - 1)
+    payload = cache.snapshot_bytes(L)
+    print(json.dumps({"case": "snapshot", "shape": a.shape, "len": L, "layers": layers,
+                      "payload_bytes": payload, "snapshot_ms": snap_ms, "restore_ms": rest_ms,
+                      "snapshot_payload_gbs": payload / (snap_ms * 1e-3) / 1e9,
+                      "restore_payload_gbs": payload / (rest_ms * 1e-3) / 1e9}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["decode", "snapshot"])
+    ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
+    ap.add_argument("--seqs", type=int, default=16)
+    ap.add_argument("--len", type=int, default=8192)
+    ap.add_argument("--layers", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=5)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    {"decode": decode_case, "snapshot": snapshot_case}[a.case](a)
+
+
+if __name__ == "__main__":
+    main()
