@@ -60,6 +60,8 @@ SIGNATURES = {
     "hx_decode_workspace_bytes": (C.c_size_t, [_P, _I, _I]),
     "hx_decode_attention": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P, _I, _P,
                                  C.c_size_t, _P]),
+    "hx_decode_attention_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P, _I,
+                                         _P]),
     "hx_snapshot_bytes": (C.c_size_t, [_P, _I]),
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_kv_restore": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),

@@ -26,6 +26,7 @@
 // segment's first tile; slot (n_segments + c) holds CTA c's first piece when
 // that piece starts inside a segment.  So slots = n_segments + C.
 #include <cfloat>
+#include <mutex>
 
 #include "hx_common.cuh"
 
@@ -683,6 +684,102 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
     const size_t slots = (size_t)n_seqs * hkv + n_ctas;
     p.ws_o = static_cast<float*>(workspace);
     p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) +
+                                        slots * group * 128 * sizeof(float));
+    if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
+    return launch_decode<16>(c, p, n_ctas, s);
+}
+
+// ---------------------------------------------------------------- no-allocation variant
+//
+// For callers that cannot allocate device memory: code running inside a
+// custom allocator or an out-of-memory handler, host environments that own
+// the whole memory budget up front, or plug-in hosts that forbid cudaMalloc
+// after start-up.  Their split-K scratch comes from a fixed array compiled
+// into this library instead of a caller-supplied workspace.
+//
+// kNoAllocScratchBytes (4 MiB) is a hard limit: a call whose workspace would
+// exceed it (see hx_decode_workspace_bytes) is rejected.  Every GPU that
+// loads the library keeps this array until the process exits.
+//
+// In host code `g_decode_scratch` is only a host-side stand-in for the device
+// array, not a device address; its device address is looked up with
+// cudaGetSymbolAddress once per device, on that device's first call.  That
+// first call on a device should therefore happen before any stream capture.
+//
+// All calls share the array and it keeps the last call's contents: the decode
+// kernel writes every slot the combine step reads within the same call, so
+// nothing needs clearing, but two calls that overlap on the GPU (different
+// streams, devices aside) race on the scratch.  Kernel-side faults of this
+// entry point are not recorded in the device status word (setting that word
+// up may allocate); bounds are still checked and waits still bounded.
+namespace hx {
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+static void* noalloc_scratch_ptr()
+{
+    static std::mutex mu;
+    static void* ptrs[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
+        ptrs[dev] = p;
+    }
+    return ptrs[dev];
+}
+}  // namespace hx
+
+extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, const void* q,
+                                           int q_dtype, const int32_t* seq_ids,
+                                           const int32_t* lengths, int n_seqs, int num_q_heads,
+                                           float scale, void* out, int out_dtype,
+                                           hx_stream_t stream)
+{
+    if (!c) return fail(HX_ERR_INVALID, "null cache");
+    if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
+    if (!q || !seq_ids || !lengths || !out) return fail(HX_ERR_INVALID, "null q/seq_ids/lengths/out");
+    if (n_seqs < 0 || n_seqs > c->cfg.max_seqs)
+        return fail(HX_ERR_INVALID, "n_seqs %d outside [0, %d]", n_seqs, c->cfg.max_seqs);
+    const int hkv = c->cfg.num_kv_heads, hd = c->cfg.head_dim;
+    if (num_q_heads < hkv || num_q_heads % hkv)
+        return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
+    if ((q_dtype != HX_FP16 && q_dtype != HX_FP32) || (out_dtype != HX_FP16 && out_dtype != HX_FP32))
+        return fail(HX_ERR_INVALID, "q/out dtype");
+    if (n_seqs == 0) return HX_OK;
+    const int group = num_q_heads / hkv;
+    const int n_ctas = num_sms();
+    const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
+    if (need > kNoAllocScratchBytes)
+        return fail(HX_ERR_CAPACITY,
+                    "this call needs %zu bytes of split-K scratch; the no-allocation entry point "
+                    "holds at most %zu (use hx_decode_attention with a caller workspace)",
+                    need, kNoAllocScratchBytes);
+    void* scratch = noalloc_scratch_ptr();
+    if (!scratch) return fail(HX_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch failed");
+    DecodeParams p{};
+    p.view = make_view(c, layer);
+    p.q = q;
+    p.q_f32 = q_dtype == HX_FP32;
+    p.seq_ids = seq_ids;
+    p.lengths = lengths;
+    p.n_seqs = n_seqs;
+    p.hq = num_q_heads;
+    p.group = group;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.out_f32 = out_dtype == HX_FP32;
+    p.status = nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (!(c->has_tmap && hd == 128 && group <= 16)) {
+        decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
+        return check_launch("decode_generic_kernel");
+    }
+    const size_t slots = (size_t)n_seqs * hkv + n_ctas;
+    p.ws_o = static_cast<float*>(scratch);
+    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(scratch) +
                                         slots * group * 128 * sizeof(float));
     if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
     return launch_decode<16>(c, p, n_ctas, s);

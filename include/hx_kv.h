@@ -183,6 +183,22 @@ int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int 
                         int num_q_heads, float scale, void* out, int out_dtype, void* workspace,
                         size_t workspace_bytes, hx_stream_t stream);
 
+/* The same decode attention as hx_decode_attention, for callers that cannot
+ * allocate device memory (code inside an allocator or an out-of-memory
+ * handler, hosts that reserve all device memory up front, plug-in hosts that
+ * forbid cudaMalloc): no workspace argument, and no cudaMalloc, cudaFree or
+ * other allocating call.  No counterpart exists in the reference engine.
+ * Its split-K scratch is a fixed 4 MiB array inside the library, which every
+ * GPU that loads the library keeps until exit; calls needing more
+ * (hx_decode_workspace_bytes > 4 MiB) fail with HX_ERR_CAPACITY.  The first
+ * call on each device looks up the array's device address, so make it before
+ * any stream capture.  All calls share the array: calls that overlap on the
+ * GPU race.  Kernel-side faults are not recorded in the device status word. */
+int hx_decode_attention_noalloc(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
+                                const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                                int num_q_heads, float scale, void* out, int out_dtype,
+                                hx_stream_t stream);
+
 /* ------------------------------------------------------------ prefix snapshots */
 
 /* Bytes of a snapshot of the first prefix_len positions of one sequence:
