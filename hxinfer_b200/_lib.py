@@ -62,6 +62,7 @@ SIGNATURES = {
                                  C.c_size_t, _P]),
     "hx_decode_attention_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P, _I,
                                          _P]),
+    "hx_prefill_attention": (_I, [_P, _I, _P, _I, _I, _I, _I, C.c_float, _P, _I, _P]),
     "hx_snapshot_bytes": (C.c_size_t, [_P, _I]),
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_kv_restore": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),

@@ -1,5 +1,6 @@
 // decode_attention.cu — K2: split-K (flash-decoding) GQA/MHA decode attention
-// over the paged head-major KV cache, plus its combine step.
+// over the paged head-major KV cache, with the split-K combine in the same
+// launch.
 //
 // Replaces attention_score_kernel(_fp16) (hxinfer-engine/src/op/cuda/
 // attention_score_cuda.cu:17-83, 95-161): there one CTA per q head walks all
@@ -20,12 +21,17 @@
 //  * At the end of each piece (the part of a segment inside one CTA) the four
 //    warps merge in shared memory.  A piece that is a whole segment writes
 //    the normalised output; otherwise it writes (O, m, l) to a workspace slot
-//    and the combine kernel merges the pieces by log-sum-exp.
+//    and counts itself in the segment's ticket; the CTA whose piece completes
+//    the segment merges all its pieces by log-sum-exp and writes the output
+//    (no second launch).
 //
-// Workspace slots: slot (seq*hkv + kv_head) holds the piece that starts at a
+// Workspace: slot (seq*hkv + kv_head) holds the piece that starts at a
 // segment's first tile; slot (n_segments + c) holds CTA c's first piece when
-// that piece starts inside a segment.  So slots = n_segments + C.
+// that piece starts inside a segment, so slots = n_segments + C.  Tickets are
+// tagged with a per-call generation number, so neither slots nor tickets need
+// clearing between calls (a fresh or stale ticket restarts the count).
 #include <cfloat>
+#include <atomic>
 #include <mutex>
 
 #include "hx_common.cuh"
@@ -38,6 +44,7 @@ constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kHalfTileBytes = 64 * 64 * 2;       // one 64x64 fp16 TMA box
 constexpr int kTileBytes = 2 * kHalfTileBytes;     // 64 positions x 128 dims
 constexpr uint32_t kStageTxBytes = 2 * kTileBytes; // K + V
+constexpr int kMaxPieces = 224;  // bound on split-K pieces per segment (needs C + 2 <= it)
 
 struct DecodeParams {
     KVView view;
@@ -50,6 +57,8 @@ struct DecodeParams {
     int out_f32;
     float* ws_o;               // [slots][group][128]
     float2* ws_ml;             // [slots][group] (m, l)
+    unsigned long long* tickets;  // [n_seqs*hkv]: (generation << 32) | pieces arrived
+    uint32_t gen;              // this call's generation tag (never 0)
     int* status;
 };
 
@@ -61,7 +70,8 @@ struct DecodeSmem {
     float merge_l[kDecConsumerWarps][ROWS];
     uint64_t full[kDecStages];
     uint64_t empty[kDecStages];
-    long long sched[4];        // first seq index, kv head, tile, tile count
+    long long sched[6];        // first seq index, kv head, tile, tile count, first tile, total
+    int flag;                  // piece-combine broadcast
 };
 
 __device__ __forceinline__ int tiles_of(int len) { return (len + kBlockTokens - 1) / kBlockTokens; }
@@ -140,6 +150,142 @@ __device__ long long locate_range(const DecodeParams& p, int cta, int n_ctas, Cu
     return total;
 }
 
+__device__ __forceinline__ long long cta_start(long long c, long long total, int n_ctas)
+{
+    return total * c / n_ctas;
+}
+
+// The CTA whose tile range [start(c), start(c+1)) holds global tile g.
+__device__ __forceinline__ int cta_of_tile(long long g, long long total, int n_ctas)
+{
+    long long c = g * n_ctas / total;
+    while (c + 1 < n_ctas && cta_start(c + 1, total, n_ctas) <= g) ++c;
+    while (c > 0 && cta_start(c, total, n_ctas) > g) --c;
+    return (int)c;
+}
+
+__device__ __forceinline__ void store_out(const DecodeParams& p, int s, int h, int r, int d, float val)
+{
+    const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
+    if (p.out_f32)
+        static_cast<float*>(p.out)[oi] = val;
+    else
+        static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+}
+
+// Counts this piece in the segment's ticket and returns the pieces seen so
+// far in this call.  A ticket holding another generation is stale (an
+// earlier call, or fresh memory) and restarts at one.
+__device__ __forceinline__ uint32_t ticket_arrive(unsigned long long* t, uint32_t gen)
+{
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(t), seen;
+    do {
+        seen = old;
+        const unsigned long long cnt = (uint32_t)(seen >> 32) == gen ? (seen & 0xffffffffull) : 0ull;
+        old = atomicCAS(t, seen, ((unsigned long long)gen << 32) | (cnt + 1));
+    } while (old != seen);
+    const unsigned long long cnt = (uint32_t)(seen >> 32) == gen ? (seen & 0xffffffffull) : 0ull;
+    return (uint32_t)(cnt + 1);
+}
+
+// Log-sum-exp merge of every piece of segment (s, h) by the 128 consumer
+// threads.  Pieces: slot `seg` (the one starting at the segment's first tile),
+// then slot n_seg + c for each CTA c whose non-empty range starts inside the
+// segment, in increasing c (at most C + 1 <= kMaxPieces pieces).  Step 1: each
+// warp takes rows r = warp (mod 4) and spreads the pieces over its lanes to get
+// the row's max and normaliser; the normalised per-piece weights go to shared
+// memory.  Step 2, per row: thread (q, d4) sums every fourth piece for dims
+// 4*d4..4*d4+3 with float4 loads, 8 in flight, and the four partial sums meet
+// in shared memory.  `scratch` (the merge buffer, 4*ROWS*128 floats) holds
+// the slot list, the weights and the partial sums:
+// kMaxPieces + ROWS*kMaxPieces + 512 floats.
+template <int ROWS>
+__device__ void combine_segment(const DecodeParams& p, int seg, int s, int h, int c_first,
+                                int c_last, long long total, int n_ctas, int n_seg, float* scratch)
+{
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    int* slot_list = reinterpret_cast<int*>(scratch);
+    float* weights = scratch + kMaxPieces;
+    static_assert(kMaxPieces + ROWS * kMaxPieces + 512 <= kDecConsumerWarps * ROWS * 128,
+                  "combine scratch exceeds the merge buffer");
+    float4* partial = reinterpret_cast<float4*>(scratch + kMaxPieces + ROWS * kMaxPieces);
+    if (t == 0) {
+        int np = 0;
+        slot_list[np++] = seg;
+        for (int c = c_first + 1; c <= c_last && np < kMaxPieces - 1; ++c)
+            if (cta_start(c + 1, total, n_ctas) > cta_start(c, total, n_ctas)) slot_list[np++] = n_seg + c;
+        slot_list[kMaxPieces - 1] = np;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+    const int np = slot_list[kMaxPieces - 1];
+    for (int r = warp; r < p.group; r += kDecConsumerWarps) {
+        float M = -INFINITY;
+        for (int q = lane; q < np; q += 32)
+            M = fmaxf(M, __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r].x));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f;
+        for (int q = lane; q < np; q += 32) {
+            const float2 ml = __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r]);
+            const float w = fast_exp2(ml.x - Mu);
+            weights[r * kMaxPieces + q] = w;
+            L += w * ml.y;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = 1.f / L;
+        __syncwarp();
+        for (int q = lane; q < np; q += 32) weights[r * kMaxPieces + q] *= inv;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+    const int d4 = lane, qoff = warp;
+    for (int r = 0; r < p.group; ++r) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q0 = qoff; q0 < np; q0 += 4 * 8) {
+            float4 v[8];
+            float w[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int q = q0 + 4 * u;
+                w[u] = q < np ? weights[r * kMaxPieces + q] : 0.f;
+                v[u] = q < np ? __ldcg(reinterpret_cast<const float4*>(
+                                    p.ws_o + ((int64_t)slot_list[q] * p.group + r) * 128) + d4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                acc.x += w[u] * v[u].x;
+                acc.y += w[u] * v[u].y;
+                acc.z += w[u] * v[u].z;
+                acc.w += w[u] * v[u].w;
+            }
+        }
+        partial[qoff * 32 + d4] = acc;
+        asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+        const float* pf = reinterpret_cast<const float*>(partial);
+        store_out(p, s, h, r, t, pf[t] + pf[128 + t] + pf[256 + t] + pf[384 + t]);
+        asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+    }
+}
+
+// Sequences with no positions attend to nothing: their rows are zeros.
+__device__ void zero_empty_outputs(const DecodeParams& p)
+{
+    const int lane = threadIdx.x & 31;
+    for (int s = 0; s < p.n_seqs; ++s) {
+        const int len = p.lengths[s];
+        if (len >= 1 && len <= p.view.capacity) continue;
+        if (lane == 0) record_status(p.status, HX_ERR_CAPACITY);
+        if (len >= 1) continue;  // over capacity: clamped, still attended
+        for (int e = lane; e < p.hq * 128; e += 32) {
+            const int64_t oi = (int64_t)s * p.hq * 128 + e;
+            if (p.out_f32) static_cast<float*>(p.out)[oi] = 0.f;
+            else static_cast<__half*>(p.out)[oi] = __float2half_rn(0.f);
+        }
+    }
+}
+
 template <int ROWS>
 __global__ void __launch_bounds__(kDecThreads, 1)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -162,16 +308,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (warp == kDecConsumerWarps) {
         Cursor c{};
         long long count = 0;
-        locate_range(p, cta, n_ctas, c, count);
+        const long long total = locate_range(p, cta, n_ctas, c, count);
         if (lane == 0) {
             sm.sched[0] = c.s;
             sm.sched[1] = c.h;
             sm.sched[2] = c.j;
             sm.sched[3] = count;
+            sm.sched[4] = total * cta / n_ctas;
+            sm.sched[5] = total;
         }
+        if (cta == 0) zero_empty_outputs(p);
     }
     __syncthreads();
     const long long count = sm.sched[3];
+    const long long g_first = sm.sched[4], total_tiles = sm.sched[5];
     if (count <= 0) return;
     Cursor cur{};
     cursor_load(cur, p, (int)sm.sched[0]);
@@ -417,8 +567,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
             const int d = threadIdx.x;  // 0..127
-            const bool whole = piece_from_seg_start && seg_end;
-            const int slot = piece_from_seg_start ? (cur.s * p.view.hkv + cur.h) : (n_seg + cta);
+            // global tile range [a, b) of this segment and the CTAs that share it
+            const long long a = g_first + i - cur.j, b = a + cur.tiles;
+            const int c_first = cta_of_tile(a, total_tiles, n_ctas);
+            const int c_last = cta_of_tile(b - 1, total_tiles, n_ctas);
+            const bool whole = c_first == c_last;
+            const int seg = cur.s * p.view.hkv + cur.h;
+            const int slot = piece_from_seg_start ? seg : (n_seg + cta);
             for (int r = 0; r < p.group; ++r) {
                 float M = -INFINITY;
 #pragma unroll
@@ -432,96 +587,33 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     acc += wgt * sm.merge_o[ww][r][d];
                 }
                 if (whole) {
-                    const float val = acc / L;
-                    const int64_t oi = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group + r) * 128 + d;
-                    if (p.out_f32)
-                        static_cast<float*>(p.out)[oi] = val;
-                    else
-                        static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+                    store_out(p, cur.s, cur.h, r, d, acc / L);
                 } else {
                     p.ws_o[((int64_t)slot * p.group + r) * 128 + d] = acc;
                     if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
                 }
             }
+            if (!whole) {
+                // Publish this piece; the CTA whose piece completes the
+                // segment merges all of them (fixed order: deterministic).
+                __threadfence();
+                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                if (d == 0) {
+                    int n_pieces = 0;
+                    for (int c = c_first; c <= c_last; ++c)
+                        n_pieces += cta_start(c + 1, total_tiles, n_ctas) > cta_start(c, total_tiles, n_ctas);
+                    sm.flag = ticket_arrive(p.tickets + seg, p.gen) == (uint32_t)n_pieces;
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                if (sm.flag) {
+                    __threadfence();
+                    combine_segment<ROWS>(p, seg, cur.s, cur.h, c_first, c_last, total_tiles, n_ctas,
+                                    n_seg, &sm.merge_o[0][0][0]);
+                }
+            }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
         }
         cursor_next(cur, p);
-    }
-}
-
-// One CTA (128 threads, one per dim) per (sequence, kv head): merges the
-// pieces of segments that more than one CTA worked on.
-__global__ void __launch_bounds__(128)
-    decode_combine_kernel(const DecodeParams p, int n_ctas)
-{
-    const int seg = blockIdx.x;
-    const int s = seg / p.view.hkv, h = seg % p.view.hkv;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __shared__ long long sh[3];
-    if (warp == 0) {
-        // global tile range [a, b) of this segment and the total T
-        long long before = 0, total = 0;
-        for (int base = 0; base < p.n_seqs; base += 32) {
-            int si = base + lane;
-            long long t = si < p.n_seqs ? tiles_of(clamp_len(p.lengths[si], p.view.capacity)) : 0;
-            long long tb = si < s ? t : 0;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                t += __shfl_xor_sync(0xffffffffu, t, o);
-                tb += __shfl_xor_sync(0xffffffffu, tb, o);
-            }
-            total += t;
-            before += tb;
-        }
-        if (lane == 0) {
-            const int tiles = tiles_of(clamp_len(p.lengths[s], p.view.capacity));
-            const long long a = (before * p.view.hkv) + (long long)h * tiles;
-            sh[0] = a;
-            sh[1] = a + tiles;
-            sh[2] = total * p.view.hkv;
-            if (p.lengths[s] < 1 || p.lengths[s] > p.view.capacity) record_status(p.status, HX_ERR_CAPACITY);
-        }
-    }
-    __syncthreads();
-    const long long a = sh[0], b = sh[1], T = sh[2];
-    const int d = threadIdx.x;
-    const int n_seg = p.n_seqs * p.view.hkv;
-    auto cstart = [&](long long c) { return T * c / n_ctas; };
-    if (a == b) {  // empty sequence: defined output of zeros
-        for (int r = 0; r < p.group; ++r) {
-            const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
-            if (p.out_f32) static_cast<float*>(p.out)[oi] = 0.f;
-            else static_cast<__half*>(p.out)[oi] = __float2half_rn(0.f);
-        }
-        return;
-    }
-    // CTAs whose (non-empty) range starts strictly inside (a, b)
-    long long c_lo = a * n_ctas / T;
-    bool any = false;
-    for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c)
-        if (cstart(c) > a && cstart(c + 1) > cstart(c)) { any = true; break; }
-    if (!any) return;  // one piece: the decode kernel wrote the output
-    for (int r = 0; r < p.group; ++r) {
-        float M = p.ws_ml[(int64_t)seg * p.group + r].x;
-        for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c)
-            if (cstart(c) > a && cstart(c + 1) > cstart(c))
-                M = fmaxf(M, p.ws_ml[(int64_t)(n_seg + c) * p.group + r].x);
-        float2 ml = p.ws_ml[(int64_t)seg * p.group + r];
-        float wgt = fast_exp2(ml.x - M);
-        float L = wgt * ml.y;
-        float acc = wgt * p.ws_o[((int64_t)seg * p.group + r) * 128 + d];
-        for (long long c = c_lo; c < n_ctas && cstart(c) < b; ++c) {
-            if (!(cstart(c) > a && cstart(c + 1) > cstart(c))) continue;
-            const int64_t slot = n_seg + c;
-            ml = p.ws_ml[slot * p.group + r];
-            wgt = fast_exp2(ml.x - M);
-            L += wgt * ml.y;
-            acc += wgt * p.ws_o[(slot * p.group + r) * 128 + d];
-        }
-        const float val = acc / L;
-        const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
-        if (p.out_f32) static_cast<float*>(p.out)[oi] = val;
-        else static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
     }
 }
 
@@ -606,7 +698,29 @@ __global__ void __launch_bounds__(128)
 static size_t decode_ws_bytes(int n_seqs, int hkv, int group, int n_ctas)
 {
     const size_t slots = (size_t)n_seqs * hkv + n_ctas;
-    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2);
+    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2) +
+           (size_t)n_seqs * hkv * sizeof(unsigned long long);
+}
+
+// Layout of the workspace: [ws_o][ws_ml][tickets].
+static void bind_workspace(DecodeParams& p, void* ws, int n_ctas)
+{
+    const size_t slots = (size_t)p.n_seqs * p.view.hkv + n_ctas;
+    char* base = static_cast<char*>(ws);
+    p.ws_o = reinterpret_cast<float*>(base);
+    base += slots * p.group * 128 * sizeof(float);
+    p.ws_ml = reinterpret_cast<float2*>(base);
+    base += slots * p.group * sizeof(float2);
+    p.tickets = reinterpret_cast<unsigned long long*>(base);
+}
+
+static std::atomic<uint32_t> g_generation{0};
+
+static uint32_t next_generation()
+{
+    uint32_t g = ++g_generation;
+    if (g == 0) g = ++g_generation;
+    return g;
 }
 
 template <int ROWS>
@@ -623,9 +737,7 @@ static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas
         attr_set[dev] = true;
     }
     decode_attention_kernel<ROWS><<<n_ctas, kDecThreads, smem, stream>>>(c->tm_k, c->tm_v, p);
-    if (int rc = check_launch("decode_attention_kernel")) return rc;
-    decode_combine_kernel<<<p.n_seqs * p.view.hkv, 128, 0, stream>>>(p, n_ctas);
-    return check_launch("decode_combine_kernel");
+    return check_launch("decode_attention_kernel");
 }
 
 }  // namespace hx
@@ -637,7 +749,7 @@ extern "C" size_t hx_decode_workspace_bytes(const hx_kv_cache* c, int n_seqs, in
     if (!c || n_seqs < 1 || num_q_heads < 1) return 0;
     const int hkv = c->cfg.num_kv_heads;
     const int group = num_q_heads / hkv;
-    return decode_ws_bytes(n_seqs, hkv, group < 1 ? 1 : group, num_sms());
+    return decode_ws_bytes(n_seqs, hkv, group < 1 ? 1 : group, std::min(num_sms(), kMaxPieces - 2));
 }
 
 extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
@@ -676,15 +788,13 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
         decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
         return check_launch("decode_generic_kernel");
     }
-    const int n_ctas = num_sms();
+    const int n_ctas = std::min(num_sms(), kMaxPieces - 2);
     const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
     if (!workspace || workspace_bytes < need)
         return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
                     workspace_bytes, need);
-    const size_t slots = (size_t)n_seqs * hkv + n_ctas;
-    p.ws_o = static_cast<float*>(workspace);
-    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) +
-                                        slots * group * 128 * sizeof(float));
+    bind_workspace(p, workspace, n_ctas);
+    p.gen = next_generation();
     if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
     return launch_decode<16>(c, p, n_ctas, s);
 }
@@ -707,9 +817,11 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
 // first call on a device should therefore happen before any stream capture.
 //
 // All calls share the array and it keeps the last call's contents: the decode
-// kernel writes every slot the combine step reads within the same call, so
-// nothing needs clearing, but two calls that overlap on the GPU (different
-// streams, devices aside) race on the scratch.  Kernel-side faults of this
+// kernel writes every slot its combine step reads within the same call, and
+// the per-segment tickets carry a per-call generation tag (a ticket from an
+// earlier call restarts at one), so nothing needs clearing; but two calls
+// that overlap on the GPU (different streams, devices aside) race on the
+// scratch.  Kernel-side faults of this
 // entry point are not recorded in the device status word (setting that word
 // up may allocate); bounds are still checked and waits still bounded.
 namespace hx {
@@ -750,7 +862,7 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
         return fail(HX_ERR_INVALID, "q/out dtype");
     if (n_seqs == 0) return HX_OK;
     const int group = num_q_heads / hkv;
-    const int n_ctas = num_sms();
+    const int n_ctas = std::min(num_sms(), kMaxPieces - 2);
     const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
     if (need > kNoAllocScratchBytes)
         return fail(HX_ERR_CAPACITY,
@@ -777,10 +889,8 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
         decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
         return check_launch("decode_generic_kernel");
     }
-    const size_t slots = (size_t)n_seqs * hkv + n_ctas;
-    p.ws_o = static_cast<float*>(scratch);
-    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(scratch) +
-                                        slots * group * 128 * sizeof(float));
+    bind_workspace(p, scratch, n_ctas);
+    p.gen = next_generation();
     if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
     return launch_decode<16>(c, p, n_ctas, s);
 }

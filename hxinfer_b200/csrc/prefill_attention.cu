@@ -1,0 +1,485 @@
+// prefill_attention.cu — K3: causal prefill attention on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// The reference has no prefill kernel: it runs one token per forward call
+// (hxinfer demos/bench_1024.cpp:62-70), i.e. the decode step of
+// attention_score_cuda.cu:17-83 once per prompt position.  Here one launch
+// computes, for query rows i in [0, n) at positions start + i,
+//     out[i] = softmax(q_i . K[0 .. start+i]^T * scale) V
+// over the paged cache (the rows' own K/V must already be appended).
+//
+// One CTA per (128-row query tile, q head); 192 threads:
+//   warp 4  TMA producer: Q tile once (2 boxes 128x64, 128-byte swizzle), then
+//           128-position K and V tiles (two cache blocks each) into a 2-stage
+//           ring; no multicast.
+//   warp 5  TMEM allocator (512 columns) and, lane 0, the MMA issuer:
+//           S_j = Q K_j^T  (M=128, N=128, K=16 x 8, fp16 -> fp32) into one of
+//           two TMEM S buffers, then O += P_j V_j (V as an MN-major operand)
+//           into the TMEM O accumulator; completion via tcgen05.commit.
+//   warps 0-3  softmax: thread t owns query row t; reads S_j with tcgen05.ld,
+//           applies the causal mask, keeps a running max that only moves when
+//           it rises by more than 2^8 (then O in TMEM is rescaled), writes
+//           P_j = 2^(s - m) as fp16 into 128-byte-swizzled shared memory (the
+//           A operand of the next MMA), and in the end divides O by the row sum.
+// Key tiles above the diagonal are never loaded.  Every mbarrier wait is
+// bounded; TMEM is always released before exit.
+#include "hx_common.cuh"
+
+namespace hx {
+
+constexpr int kPfThreads = 192;
+constexpr int kRegionBytes = 128 * 128;  // 128 rows x 64 fp16 (one 128-byte swizzled region)
+
+struct PrefillParams {
+    KVView view;
+    int seq, start, n, hq, group, n_qtiles;
+    float scale_log2;
+    void* out;
+    int out_f32;
+    int* status;
+};
+
+struct PrefillSmem {
+    uint8_t q[2][kRegionBytes];        // [d half]
+    uint8_t k[2][2][kRegionBytes];     // [stage][d half]
+    uint8_t v[2][2][kRegionBytes];     // [stage][d half]
+    uint8_t p[2][kRegionBytes];        // [key half]
+    uint64_t q_full;
+    uint64_t kv_full[2], kv_empty[2];
+    uint64_t s_full[2], s_free[2];
+    uint64_t p_full, pv_done, mma_idle;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+// ------------------------------------------------------------ tcgen05 helpers
+
+// Shared-memory matrix descriptor: start, leading / stride byte offsets,
+// version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, fp16 A and B,
+// M = 128, N = 128; b_mn selects an MN-major B operand.
+__device__ __forceinline__ uint32_t umma_idesc(bool b_mn)
+{
+    return (1u << 4) | ((b_mn ? 1u : 0u) << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v)
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v)
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// A bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool pf_wait(PrefillSmem& sm, uint64_t* bar, uint32_t parity, int* status)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) return false;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            record_status(status, HX_ERR_TIMEOUT);
+            atomicExch(&sm.abort_flag, 1);
+            return false;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const PrefillParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // longest tiles first
+    const int h = blockIdx.y, kvh = h / p.group;
+    const int q0 = qt * 128;
+    const int rows_valid = min(128, p.n - q0);
+    const int kend = p.start + q0 + rows_valid;  // keys [0, kend) are needed by this tile
+    const int nk = (kend + 127) / 128;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.kv_full[i], 1);
+            mbar_init(&sm.kv_empty[i], 1);
+            mbar_init(&sm.s_full[i], 1);
+            mbar_init(&sm.s_free[i], 4);
+        }
+        mbar_init(&sm.p_full, 4);
+        mbar_init(&sm.pv_done, 1);
+        mbar_init(&sm.mma_idle, 1);
+        sm.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                         smem_u32(&sm.tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            mbar_arrive_expect_tx(&sm.q_full, 2 * kRegionBytes);
+            tma_load_2d(sm.q[0], &tm_q, h * 128, q0, &sm.q_full, pol);
+            tma_load_2d(sm.q[1], &tm_q, h * 128 + 64, q0, &sm.q_full, pol);
+            const KVView& v = p.view;
+            int issued = 0;
+            for (int j = 0; j < nk; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !pf_wait(sm, &sm.kv_empty[s], ((j >> 1) - 1) & 1, p.status)) break;
+                int64_t rows[2];
+                uint32_t bytes = 0;
+                for (int b = 0; b < 2; ++b) {
+                    const int blk = 2 * j + b;
+                    rows[b] = -1;
+                    if (blk * kBlockTokens >= kend) continue;
+                    const int64_t pb = phys_block(v, p.seq, blk);
+                    if (pb < 0) {
+                        record_status(p.status, HX_ERR_CAPACITY);
+                        continue;
+                    }
+                    rows[b] = (pb * v.block_stride + (int64_t)kvh * v.head_stride) / 256;
+                    bytes += 4 * (kRegionBytes / 2);
+                }
+                mbar_arrive_expect_tx(&sm.kv_full[s], bytes);
+                for (int b = 0; b < 2; ++b) {
+                    if (rows[b] < 0) continue;
+                    const int rk = (int)(v.k_row0 + rows[b]), rv = (int)(v.v_row0 + rows[b]);
+                    const int off = b * (kRegionBytes / 2);
+                    tma_load_2d(sm.k[s][0] + off, &tm_k, 0, rk, &sm.kv_full[s], pol);
+                    tma_load_2d(sm.k[s][1] + off, &tm_k, 64, rk, &sm.kv_full[s], pol);
+                    tma_load_2d(sm.v[s][0] + off, &tm_v, 0, rv, &sm.kv_full[s], pol);
+                    tma_load_2d(sm.v[s][1] + off, &tm_v, 64, rv, &sm.kv_full[s], pol);
+                }
+                issued = j + 1;
+            }
+            // Copies still in flight must land before the CTA exits (bounded).
+            mbar_wait(&sm.q_full, 0);
+            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1);
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_qk = umma_idesc(false), id_pv = umma_idesc(true);
+            bool ok = pf_wait(sm, &sm.q_full, 0, p.status);
+            for (int j = 0; ok && j <= nk; ++j) {
+                if (j < nk) {
+                    const int s = j & 1, b = j & 1;
+                    ok = pf_wait(sm, &sm.kv_full[s], (j >> 1) & 1, p.status);
+                    if (ok && j >= 2) ok = pf_wait(sm, &sm.s_free[b], ((j >> 1) - 1) & 1, p.status);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t a = umma_desc(smem_u32(sm.q[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = umma_desc(smem_u32(sm.k[s][kk >> 2]) + (kk & 3) * 32, 16, 1024);
+                        umma_f16(tmem + 128 * b, a, bd, id_qk, kk > 0);
+                    }
+                    umma_commit(&sm.s_full[b]);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, sp = jj & 1;
+                    if (!pf_wait(sm, &sm.p_full, jj & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t a = umma_desc(smem_u32(sm.p[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = umma_desc(smem_u32(sm.v[sp][0]) + kk * 2048, kRegionBytes, 1024);
+                        umma_f16(tmem + 256, a, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&sm.kv_empty[sp]);
+                    umma_commit(&sm.pv_done);
+                }
+            }
+            // Every MMA this thread issued must finish before TMEM is freed.
+            umma_commit(&sm.mma_idle);
+            if (!mbar_wait(&sm.mma_idle, 0)) record_status(p.status, HX_ERR_TIMEOUT);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax warps
+        const int t = threadIdx.x;  // query row within the tile
+        const int row_pos = p.start + q0 + t;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        float m_run = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nk; ++j) {
+            const int b = j & 1, s = j & 1;
+            if (!pf_wait(sm, &sm.s_full[b], (j >> 1) & 1, p.status)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + 128 * b + 32 * c, sv + 32 * c);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.s_free[b]);
+            const int k0 = 128 * j;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+                const float x = (k0 + c <= row_pos) ? sv[c] * p.scale_log2 : -INFINITY;
+                sv[c] = x;
+                mt = fmaxf(mt, x);
+            }
+            if (j >= 1) {
+                // P_{j-1} V_{j-1} finished: the P buffer is free and O is stable
+                if (!pf_wait(sm, &sm.pv_done, (j - 1) & 1, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+            if (mt > m_run + 8.f) {
+                const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
+                if (j >= 1 && alpha < 1.f) {
+                    const uint32_t oaddr = lane_base + 256;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float ov[32];
+                        tmem_ld32(oaddr + 32 * c, ov);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                        tmem_st32(oaddr + 32 * c, ov);
+                    }
+                    tmem_st_wait();
+                }
+                l *= alpha;
+                m_run = mt;
+            }
+            if (k0 + 128 > kend) {
+                // V rows past the last needed key may hold stale bytes: zero
+                // this thread's row so 0 * garbage cannot reach O.
+                if (!pf_wait(sm, &sm.kv_full[s], (j >> 1) & 1, p.status)) {
+                    ok = false;
+                    break;
+                }
+                if (k0 + t >= kend) {
+#pragma unroll
+                    for (int dh = 0; dh < 2; ++dh)
+#pragma unroll
+                        for (int ch = 0; ch < 8; ++ch)
+                            *reinterpret_cast<uint4*>(sm.v[s][dh] + t * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            // P row t: keys c = 64*kh + 8*ch + e at region kh, 16-byte chunk ch ^ (t & 7)
+#pragma unroll
+            for (int kh = 0; kh < 2; ++kh) {
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int c = 64 * kh + 8 * ch + 2 * e;
+                        const float p0 = fast_exp2(sv[c] - m_run), p1 = fast_exp2(sv[c + 1] - m_run);
+                        l += p0 + p1;
+                        w[e] = pack_half2(p0, p1);
+                    }
+                    *reinterpret_cast<uint4*>(sm.p[kh] + t * 128 + ((ch ^ (t & 7)) << 4)) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.p_full);
+        }
+        if (ok && pf_wait(sm, &sm.pv_done, (nk - 1) & 1, p.status)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            const bool valid = t < rows_valid;
+            const int64_t obase = ((int64_t)(q0 + t) * p.hq + h) * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float ov[32];
+                tmem_ld32(lane_base + 256 + 32 * c, ov);
+                tmem_ld_wait();
+                if (!valid) continue;
+                if (p.out_f32) {
+                    float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + 32 * c);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        o4[e] = make_float4(ov[4 * e] * inv, ov[4 * e + 1] * inv, ov[4 * e + 2] * inv,
+                                            ov[4 * e + 3] * inv);
+                } else {
+                    uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + obase + 32 * c);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        o4[e] = make_uint4(pack_half2(ov[8 * e] * inv, ov[8 * e + 1] * inv),
+                                           pack_half2(ov[8 * e + 2] * inv, ov[8 * e + 3] * inv),
+                                           pack_half2(ov[8 * e + 4] * inv, ov[8 * e + 5] * inv),
+                                           pack_half2(ov[8 * e + 6] * inv, ov[8 * e + 7] * inv));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+typedef CUresult (*EncodeTiledFnPf)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Q viewed as [n][hq*128] fp16 with 64x128 boxes, 128-byte swizzle.
+static int encode_q_map(CUtensorMap* tm, const void* q, int hq, int n)
+{
+    static EncodeTiledFnPf fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &r) !=
+                cudaSuccess ||
+            r != cudaDriverEntryPointSuccess)
+            return fail(HX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFnPf>(f);
+    }
+    cuuint64_t gdim[2] = {(cuuint64_t)hq * 128, (cuuint64_t)n};
+    cuuint64_t gstride[1] = {(cuuint64_t)hq * 256};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(q), gdim, gstride, box,
+                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(HX_ERR_CUDA, "q tensor map (%d)", (int)r);
+    return HX_OK;
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+extern "C" int hx_prefill_attention(const hx_kv_cache* c, int layer, const void* q, int seq,
+                                    int start, int n, int num_q_heads, float scale, void* out,
+                                    int out_dtype, hx_stream_t stream)
+{
+    if (!c) return fail(HX_ERR_INVALID, "null cache");
+    if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
+    if (!q || !out) return fail(HX_ERR_INVALID, "null q/out");
+    if (seq < 0 || seq >= c->cfg.max_seqs) return fail(HX_ERR_INVALID, "seq %d out of range", seq);
+    if (start < 0 || n < 0) return fail(HX_ERR_INVALID, "start/n must be >= 0");
+    if ((int64_t)start + n > (int64_t)c->n_mapped[seq] * kBlockTokens ||
+        (int64_t)start + n > c->cfg.max_tokens_per_seq)
+        return fail(HX_ERR_CAPACITY, "positions [0, %d) not reserved for seq %d", start + n, seq);
+    const int hkv = c->cfg.num_kv_heads;
+    if (num_q_heads < hkv || num_q_heads % hkv)
+        return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
+    if (c->cfg.head_dim != 128 || !c->has_tmap)
+        return fail(HX_ERR_UNSUPPORTED, "prefill attention needs head_dim 128 (got %d)", c->cfg.head_dim);
+    if (out_dtype != HX_FP16 && out_dtype != HX_FP32) return fail(HX_ERR_INVALID, "out dtype");
+    if (reinterpret_cast<uintptr_t>(q) & 15 || reinterpret_cast<uintptr_t>(out) & 15)
+        return fail(HX_ERR_INVALID, "q/out must be 16-byte aligned");
+    if (n == 0) return HX_OK;
+    CUtensorMap tm_q;
+    if (int rc = encode_q_map(&tm_q, q, num_q_heads, n)) return rc;
+    PrefillParams p{};
+    p.view = make_view(c, layer);
+    p.seq = seq;
+    p.start = start;
+    p.n = n;
+    p.hq = num_q_heads;
+    p.group = num_q_heads / hkv;
+    p.n_qtiles = (n + 127) / 128;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.out_f32 = out_dtype == HX_FP32;
+    p.status = status_word();
+    const size_t smem = sizeof(PrefillSmem) + 1024;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        HX_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_set[dev] = true;
+    }
+    dim3 grid(p.n_qtiles, num_q_heads);
+    prefill_attention_kernel<<<grid, kPfThreads, smem, (cudaStream_t)stream>>>(tm_q, c->tm_k, c->tm_v, p);
+    return check_launch("prefill_attention_kernel");
+}

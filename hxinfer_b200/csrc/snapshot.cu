@@ -3,40 +3,83 @@
 // Replaces the host std::memcpy of PrefixCacheManager::store / restore
 // (hxinfer-engine/include/cache/prefix_cache.h:78-89, 135-147), which copies
 // the first prefix_len rows of every layer's K and V.  Here one launch copies
-// all layers: 16-byte vector loads/stores (2-byte elements when head_dim*2 is
-// not a multiple of 16), grid-stride over the payload, so the copy runs at
-// HBM copy speed.  Snapshot layout: [layer][K|V][kv_head][prefix_len][head_dim]
-// fp16, dense.  Positions >= prefix_len are never read or written.
+// all layers: each (layer, K|V, kv head, block) run is contiguous in both the
+// cache and the snapshot, so a CTA streams it with 16-byte vectors (2-byte
+// elements when head_dim*2 is not a multiple of 16), streaming cache hints.
+// Snapshot layout: [layer][K|V][kv_head][prefix_len][head_dim] fp16, dense.  Positions >= prefix_len are never read or written.
 #include "hx_common.cuh"
 
 namespace hx {
 
-// One work unit = `unit` bytes of one position row of one (layer, K|V, head).
-template <typename U, bool TO_SNAPSHOT>
-__global__ void snapshot_copy_kernel(KVView v0, int64_t layer_stride, int layers, int seq,
-                                     int prefix_len, U* __restrict__ snap, int* status)
+// One work item = the positions of one block of one (layer, K|V, kv head):
+// a contiguous run of up to 64 rows in the cache and in the snapshot.  A CTA
+// copies it with every thread holding four 16-byte vectors in flight.
+// Row bytes (head_dim * 2) must be a multiple of 16 here.
+template <bool TO_SNAPSHOT>
+__global__ void __launch_bounds__(256)
+    snapshot_block_kernel(KVView v0, int64_t layer_stride, int layers, int seq, int prefix_len,
+                          uint4* __restrict__ snap, int* status)
 {
-    const int hd_bytes = v0.hd * 2;
-    const int per_row = hd_bytes / (int)sizeof(U);
-    const int64_t rows_per_plane = (int64_t)v0.hkv * prefix_len;
-    const int64_t total = (int64_t)layers * 2 * rows_per_plane * per_row;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
-        const int sub = (int)(u % per_row);
-        const int64_t row = u / per_row;
-        const int pos = (int)(row % prefix_len);
-        const int64_t hp = row / prefix_len;  // (layer, kv, head)
-        const int h = (int)(hp % v0.hkv);
-        const int64_t lkv = hp / v0.hkv;
+    const int row_vecs = v0.hd * 2 / 16;
+    const int nblk = (prefix_len + kBlockTokens - 1) / kBlockTokens;
+    const int64_t items = (int64_t)layers * 2 * v0.hkv * nblk;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+        const int blk = (int)(it % nblk);
+        const int64_t plane = it / nblk;  // (layer, kv, head)
+        const int h = (int)(plane % v0.hkv);
+        const int64_t lkv = plane / v0.hkv;
         const int kv = (int)(lkv & 1);
         const int64_t layer = lkv >> 1;
+        const int64_t pb = phys_block(v0, seq, blk);
+        if (pb < 0) {
+            if (threadIdx.x == 0) record_status(status, HX_ERR_CAPACITY);
+            continue;
+        }
+        const int rows = min(kBlockTokens, prefix_len - blk * kBlockTokens);
+        const int nvec = rows * row_vecs;
+        uint4* cache = reinterpret_cast<uint4*>((kv ? v0.v : v0.k) + layer * layer_stride +
+                                                pb * v0.block_stride + (int64_t)h * v0.head_stride);
+        uint4* dst = snap + (plane * prefix_len + (int64_t)blk * kBlockTokens) * row_vecs;
+        uint4* from = TO_SNAPSHOT ? cache : dst;
+        uint4* to = TO_SNAPSHOT ? dst : cache;
+        for (int base = 0; base < nvec; base += 4 * 256) {
+            uint4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * 256 + threadIdx.x;
+                if (e < nvec) x[u] = __ldcs(from + e);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * 256 + threadIdx.x;
+                if (e < nvec) __stcs(to + e, x[u]);
+            }
+        }
+    }
+}
+
+// Any even head_dim: one 2-byte element per work unit.
+template <bool TO_SNAPSHOT>
+__global__ void snapshot_elem_kernel(KVView v0, int64_t layer_stride, int layers, int seq,
+                                     int prefix_len, uint16_t* __restrict__ snap, int* status)
+{
+    const int hd = v0.hd;
+    const int64_t total = (int64_t)layers * 2 * v0.hkv * prefix_len * hd;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
+        const int d = (int)(u % hd);
+        const int64_t row = u / hd;
+        const int pos = (int)(row % prefix_len);
+        const int64_t plane = row / prefix_len;
+        const int h = (int)(plane % v0.hkv);
+        const int64_t lkv = plane / v0.hkv;
         const int64_t off = token_offset(v0, seq, h, pos);
         if (off < 0) {
             record_status(status, HX_ERR_CAPACITY);
             continue;
         }
-        char* base = (kv ? v0.v : v0.k) + layer * layer_stride + off;
-        U* cache = reinterpret_cast<U*>(base) + sub;
+        uint16_t* cache = reinterpret_cast<uint16_t*>(((lkv & 1) ? v0.v : v0.k) +
+                                                      (lkv >> 1) * layer_stride + off) + d;
         if (TO_SNAPSHOT)
             snap[u] = *cache;
         else
@@ -50,18 +93,19 @@ static int launch_copy(const hx_kv_cache* c, int seq, int prefix_len, void* buf,
 {
     KVView v = make_view(c, 0);
     const int hd_bytes = c->cfg.head_dim * 2;
-    const int64_t bytes = (int64_t)c->cfg.num_layers * 2 * c->cfg.num_kv_heads * prefix_len * hd_bytes;
-    const int unit = (hd_bytes % 16 == 0) ? 16 : 2;
-    const int64_t units = bytes / unit;
-    int blocks = (int)std::min<int64_t>((units + 255) / 256, (int64_t)num_sms() * 16);
-    if (blocks < 1) blocks = 1;
-    if (unit == 16)
-        snapshot_copy_kernel<uint4, TO_SNAPSHOT><<<blocks, 256, 0, stream>>>(
+    if (hd_bytes % 16 == 0) {
+        const int nblk = (prefix_len + kBlockTokens - 1) / kBlockTokens;
+        const int64_t items = (int64_t)c->cfg.num_layers * 2 * c->cfg.num_kv_heads * nblk;
+        const int blocks = (int)std::min<int64_t>(items, (int64_t)num_sms() * 16);
+        snapshot_block_kernel<TO_SNAPSHOT><<<blocks, 256, 0, stream>>>(
             v, c->layer_stride, c->cfg.num_layers, seq, prefix_len, (uint4*)buf, status_word());
-    else
-        snapshot_copy_kernel<uint16_t, TO_SNAPSHOT><<<blocks, 256, 0, stream>>>(
-            v, c->layer_stride, c->cfg.num_layers, seq, prefix_len, (uint16_t*)buf, status_word());
-    return check_launch("snapshot_copy_kernel");
+        return check_launch("snapshot_block_kernel");
+    }
+    const int64_t units = (int64_t)c->cfg.num_layers * 2 * c->cfg.num_kv_heads * prefix_len * c->cfg.head_dim;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, (int64_t)num_sms() * 16));
+    snapshot_elem_kernel<TO_SNAPSHOT><<<blocks, 256, 0, stream>>>(
+        v, c->layer_stride, c->cfg.num_layers, seq, prefix_len, (uint16_t*)buf, status_word());
+    return check_launch("snapshot_elem_kernel");
 }
 
 }  // namespace hx

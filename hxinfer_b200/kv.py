@@ -195,6 +195,21 @@ class KVCache:
                                          _stream(stream)), "decode attention")
         return out
 
+    def prefill(self, layer: int, q: torch.Tensor, seq: int, start: int, num_q_heads: int, *,
+                scale: float | None = None, out: torch.Tensor | None = None,
+                out_dtype=torch.float16, stream=None):
+        """Causal attention of q rows [n, Hq*hd] at positions start..start+n-1."""
+        _need_cuda(q, out)
+        n = q.numel() // (num_q_heads * self.head_dim)
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            out = torch.empty((n, num_q_heads * self.head_dim), dtype=out_dtype, device=q.device)
+        check(load().hx_prefill_attention(self.handle, layer, _ptr(q), seq, start, n, num_q_heads,
+                                          scale, _ptr(out), _dt(out), _stream(stream)),
+              "prefill attention")
+        return out
+
     def snapshot_bytes(self, prefix_len: int) -> int:
         return int(load().hx_snapshot_bytes(self.handle, prefix_len))
 

@@ -3,6 +3,7 @@
     python -m hxinfer_b200.profile_case decode  --shape llama3 --seqs 16 --len 8192 --layers 1 --iters 5
     python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
+    python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
 
 Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
 prints one JSON line with the CUDA-event time per iteration and the
@@ -92,17 +93,49 @@ def snapshot_case(a):
                       "restore_payload_gbs": payload / (rest_ms * 1e-3) / 1e9}))
 
 
+def prefill_case(a):
+    """Causal prefill of `len` fresh tokens (start 0), all q heads of the shape."""
+    hq, hkv, theta = SHAPES[a.shape]
+    hd, n = 128, a.len
+    cache = kv.KVCache(a.layers, hkv, hd, 1, n + a.start)
+    cache.reserve(0, n + a.start)
+    cache.fill_normal(11)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    q = torch.randn((n, hq * hd), generator=g, device="cuda").half()
+    out = torch.empty_like(q)
+    evs = []
+    for it in range(a.iters):
+        for l in range(a.layers):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            cache.prefill(l, q, 0, a.start, hq, out=out)
+            e1.record()
+            evs.append((e0, e1))
+    torch.cuda.synchronize()
+    kv.device_status()
+    ms = [x.elapsed_time(y) for x, y in evs[a.layers:]] or [evs[0][0].elapsed_time(evs[0][1])]
+    avg = sum(ms) / len(ms)
+    # unmasked (query, key) pairs x 4 flops per pair per dim
+    pairs = sum(a.start + i + 1 for i in range(n))
+    flops = 4.0 * hq * hd * pairs
+    print(json.dumps({"case": "prefill", "shape": a.shape, "len": n, "start": a.start,
+                      "layers": a.layers, "prefill_ms_avg": avg, "flops_per_launch": flops,
+                      "tflops": flops / (avg * 1e-3) / 1e12}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill"])
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
     ap.add_argument("--len", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--start", type=int, default=0)
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    {"decode": decode_case, "snapshot": snapshot_case}[a.case](a)
+    {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case}[a.case](a)
 
 
 if __name__ == "__main__":

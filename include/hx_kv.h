@@ -183,6 +183,18 @@ int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int 
                         int num_q_heads, float scale, void* out, int out_dtype, void* workspace,
                         size_t workspace_bytes, hx_stream_t stream);
 
+/* K3: causal prefill attention on the tcgen05 tensor cores.  Query rows
+ * i in [0, n) sit at positions start + i of sequence `seq` and attend to
+ * positions [0, start + i] of the cache (their own K/V must already be
+ * appended, e.g. by hx_rope_append).  q: device fp16 [n][num_q_heads*128]
+ * (rotated), 16-byte aligned; out: [n][num_q_heads*128] in out_dtype.
+ * head_dim must be 128.  The reference prefills one token per forward call
+ * (hxinfer demos/bench_1024.cpp:62-70), i.e. attention_score_cuda.cu:17-83 once
+ * per position; this is the same function of the inputs in one launch. */
+int hx_prefill_attention(const hx_kv_cache* cache, int layer, const void* q, int seq, int start,
+                         int n, int num_q_heads, float scale, void* out, int out_dtype,
+                         hx_stream_t stream);
+
 /* The same decode attention as hx_decode_attention, for callers that cannot
  * allocate device memory (code inside an allocator or an out-of-memory
  * handler, hosts that reserve all device memory up front, plug-in hosts that

@@ -210,6 +210,54 @@ def test_decode_batched_llama3(hx, oracle):
     run_decode(hx, oracle, 32, 8, [int(x) for x in lengths], seed=44)
 
 
+def test_decode_repeated_calls_share_workspace(hx, oracle):
+    """Split-K pieces meet through generation-tagged tickets in the workspace:
+    repeated calls on one workspace (no clearing) give identical outputs."""
+    rng = np.random.default_rng(60)
+    Hq, Hkv, lengths = 28, 4, [32769, 1025, 70]
+    cache = make_cache(hx, 1, Hkv, 3, 32769)
+    for s, L in enumerate(lengths):
+        cache.reserve(s, L)
+    cache.fill_normal(61)
+    q = torch.from_numpy(rng.standard_normal((3, Hq * 128)).astype(np.float16)).cuda()
+    sid = torch.arange(3, dtype=torch.int32, device="cuda")
+    lens = dev(np.array(lengths, np.int32))
+    ws = torch.empty(cache.workspace_bytes(3, Hq), dtype=torch.uint8, device="cuda")
+    outs = [cache.decode(0, q, sid, lens, Hq, workspace=ws).clone() for _ in range(3)]
+    torch.cuda.synchronize()
+    hx.device_status()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+    k, v = cache.read(0, 0, 0, lengths[0])
+    want = oracle.decode_attention(q[0].float().cpu().numpy(), k.reshape(lengths[0], -1).float().cpu().numpy(),
+                                   v.reshape(lengths[0], -1).float().cpu().numpy(), Hq, Hkv, 128)
+    assert_close(outs[0][0].float().cpu().numpy(), want, "32k after repeats")
+
+
+def test_decode_zero_length_sequence(hx, oracle):
+    """A sequence with no positions gets zeros and the status word records it;
+    its neighbours are unaffected."""
+    rng = np.random.default_rng(62)
+    Hq, Hkv = 32, 8
+    cache = make_cache(hx, 1, Hkv, 3, 256)
+    for s in range(3):
+        cache.reserve(s, 256)
+    cache.fill_normal(63)
+    q = torch.from_numpy(rng.standard_normal((3, Hq * 128)).astype(np.float16)).cuda()
+    lens = dev(np.array([100, 0, 200], np.int32))
+    out = cache.decode(0, q, torch.arange(3, dtype=torch.int32, device="cuda"), lens, Hq)
+    torch.cuda.synchronize()
+    from hxinfer_b200._lib import HXError
+    with pytest.raises(HXError):
+        hx.device_status(clear=True)
+    assert torch.count_nonzero(out[1]) == 0
+    for s, L in ((0, 100), (2, 200)):
+        k, v = cache.read(0, s, 0, L)
+        want = oracle.decode_attention(q[s].float().cpu().numpy(), k.reshape(L, -1).float().cpu().numpy(),
+                                       v.reshape(L, -1).float().cpu().numpy(), Hq, Hkv, 128)
+        assert_close(out[s].float().cpu().numpy(), want, f"seq {s}")
+
+
 @pytest.mark.parametrize("hd", [64, 2])
 def test_decode_generic_head_dim(hx, oracle, hd):
     run_decode(hx, oracle, 4, 2, [1, 70, 200], hd=hd, seed=hd)
@@ -314,6 +362,29 @@ def test_snapshot_restore_bit_exact(hx):
         assert torch.equal(v2[:plen].view(torch.int16), before[l][1][:plen].view(torch.int16))
         assert torch.equal(k2[plen:].view(torch.int16), other[l][0][plen:].view(torch.int16))
         assert torch.equal(v2[plen:].view(torch.int16), other[l][1][plen:].view(torch.int16))
+
+
+@pytest.mark.parametrize("plen", [1, 64, 65, 2048])
+def test_snapshot_restore_qwen_shape(hx, plen):
+    """Config-5 shape (28 layers, 4 kv heads): the snapshot equals the cache
+    rows it covers, and a restore into another sequence reproduces them."""
+    layers, Hkv = 28, 4
+    cache = make_cache(hx, layers, Hkv, 2, 2048)
+    cache.reserve(0, 2048)
+    cache.reserve(1, 2048)
+    cache.fill_normal(70 + plen)
+    snap = cache.snapshot(0, plen)
+    cache.restore(1, plen, snap)
+    torch.cuda.synchronize()
+    hx.device_status()
+    s = snap.view(torch.float16).view(layers, 2, Hkv, plen, 128)
+    for l in (0, 13, 27):
+        k0, v0 = cache.read(l, 0, 0, plen)
+        k1, v1 = cache.read(l, 1, 0, plen)
+        assert torch.equal(s[l, 0].permute(1, 0, 2).contiguous().view(torch.int16), k0.view(torch.int16))
+        assert torch.equal(s[l, 1].permute(1, 0, 2).contiguous().view(torch.int16), v0.view(torch.int16))
+        assert torch.equal(k1.view(torch.int16), k0.view(torch.int16))
+        assert torch.equal(v1.view(torch.int16), v0.view(torch.int16))
 
 
 def test_snapshot_rejects_unreserved_prefix(hx):

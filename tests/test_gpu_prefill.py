@@ -1,0 +1,72 @@
+"""K3 causal prefill (tcgen05) against the CPU oracle.
+
+Oracle: the reference prefills one token per forward call, so row i is the
+decode-step loop of attention.cpp:51-85 over positions [0, start+i]
+(oracle.prefill_attention).  Bar: |gpu - oracle| <= 2e-3 + 1e-2*|oracle|."""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+@pytest.fixture(scope="module")
+def hx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hxinfer_b200 import kv
+    kv.load()
+    kv.device_status(clear=True)
+    return kv
+
+
+def run_prefill(hx, oracle, Hq, Hkv, start, n, seed, out_dtype=torch.float16, layers=2, layer=1):
+    rng = np.random.default_rng(seed)
+    total = start + n
+    kc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
+    vc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
+    q = oracle.f16(rng.standard_normal((n, Hq * 128)))
+    cache = hx.KVCache(layers, Hkv, 128, 3, total + 64)
+    seq = 2  # not the first sequence: exercises the block table
+    cache.reserve(0, 64)
+    cache.reserve(seq, total)
+    cache.write(layer, seq, 0, torch.from_numpy(kc).half().cuda(), torch.from_numpy(vc).half().cuda())
+    out = cache.prefill(layer, torch.from_numpy(q).half().cuda(), seq, start, Hq,
+                        scale=1.0 / math.sqrt(128), out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    hx.device_status()
+    want = oracle.prefill_attention(q, kc, vc, start, Hq, Hkv, 128)
+    got = out.float().cpu().numpy()
+    err = np.abs(got - want)
+    bad = err > ATOL + RTOL * np.abs(want)
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance, max abs err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("n", [1, 5, 128, 129, 300])
+def test_prefill_small_mha(hx, oracle, n):
+    run_prefill(hx, oracle, 4, 4, 0, n, seed=n)
+
+
+def test_prefill_llama2_shape_1024(hx, oracle):
+    """Config 2's prefill: LLaMA-2-7B MHA (32 heads), 1024 tokens (8 heads here
+    for oracle time; the kernel is per head)."""
+    run_prefill(hx, oracle, 8, 8, 0, 1024, seed=2)
+
+
+def test_prefill_qwen_gqa(hx, oracle):
+    run_prefill(hx, oracle, 28, 4, 0, 200, seed=3)
+
+
+@pytest.mark.parametrize("start,n", [(2048, 256), (63, 70), (1, 1), (500, 129)])
+def test_prefill_continuation(hx, oracle, start, n):
+    """Config 5's continuation: new rows after a cached prefix."""
+    run_prefill(hx, oracle, 8, 2, start, n, seed=start + n)
+
+
+def test_prefill_fp32_out(hx, oracle):
+    run_prefill(hx, oracle, 4, 2, 10, 140, seed=9, out_dtype=torch.float32)
