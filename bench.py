@@ -228,7 +228,7 @@ def run_batched_decode(args):
     base = torch.from_numpy(my_len.astype(np.int32)).to(dev)
     pos_tab = torch.stack([base + s for s in range(total_steps)])  # append position per step
     len_tab = pos_tab + 1
-    ws = torch.empty(cache.workspace_bytes(n, hq), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(cache.workspace_bytes(n, hq), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     ev_pairs = []
 

@@ -14,12 +14,13 @@ LIB_PATH = os.path.join(PKG, "libhxkv.so")
 HX_OK, HX_ERR_INVALID, HX_ERR_CAPACITY, HX_ERR_OOM, HX_ERR_CUDA = 0, 1, 2, 3, 4
 HX_ERR_NCCL, HX_ERR_TIMEOUT, HX_ERR_NOT_FOUND, HX_ERR_UNSUPPORTED = 5, 6, 7, 8
 HX_FP32, HX_FP16 = 1, 3
+HX_KV_OVERLAP_LAUNCH = 1
 
 
 class hx_kv_config(C.Structure):
     _fields_ = [("num_layers", C.c_int32), ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32),
                 ("max_seqs", C.c_int32), ("max_tokens_per_seq", C.c_int32),
-                ("num_blocks", C.c_int64)]
+                ("num_blocks", C.c_int64), ("flags", C.c_int32)]
 
 
 class hx_kv_info(C.Structure):

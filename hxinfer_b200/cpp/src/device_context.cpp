@@ -65,6 +65,7 @@ void* workspace(size_t bytes)
         s.ws = nullptr;
         s.ws_bytes = 0;
         if (cudaMalloc(&s.ws, bytes) != cudaSuccess) return nullptr;
+        if (cudaMemset(s.ws, 0, bytes) != cudaSuccess) return nullptr;  // tickets start at zero
         s.ws_bytes = bytes;
     }
     return s.ws;

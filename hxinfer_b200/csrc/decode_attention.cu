@@ -1,6 +1,5 @@
 // decode_attention.cu — K2: split-K (flash-decoding) GQA/MHA decode attention
-// over the paged head-major KV cache, with the split-K combine in the same
-// launch.
+// over the paged head-major KV cache, and its combine kernel.
 //
 // Replaces attention_score_kernel(_fp16) (hxinfer-engine/src/op/cuda/
 // attention_score_cuda.cu:17-83, 95-161): there one CTA per q head walks all
@@ -21,17 +20,14 @@
 //  * At the end of each piece (the part of a segment inside one CTA) the four
 //    warps merge in shared memory.  A piece that is a whole segment writes
 //    the normalised output; otherwise it writes (O, m, l) to a workspace slot
-//    and counts itself in the segment's ticket; the CTA whose piece completes
-//    the segment merges all its pieces by log-sum-exp and writes the output
-//    (no second launch).
+//    and decode_combine_kernel (one CTA per segment and q row, launched as a
+//    programmatic dependent) merges the pieces by log-sum-exp.
 //
 // Workspace: slot (seq*hkv + kv_head) holds the piece that starts at a
 // segment's first tile; slot (n_segments + c) holds CTA c's first piece when
-// that piece starts inside a segment, so slots = n_segments + C.  Tickets are
-// tagged with a per-call generation number, so neither slots nor tickets need
-// clearing between calls (a fresh or stale ticket restarts the count).
+// that piece starts inside a segment, so slots = n_segments + C.  Every slot
+// the combine reads is written in the same call: nothing needs clearing.
 #include <cfloat>
-#include <atomic>
 #include <mutex>
 
 #include "hx_common.cuh"
@@ -57,9 +53,18 @@ struct DecodeParams {
     int out_f32;
     float* ws_o;               // [slots][group][128]
     float2* ws_ml;             // [slots][group] (m, l)
-    unsigned long long* tickets;  // [n_seqs*hkv]: (generation << 32) | pieces arrived
-    uint32_t gen;              // this call's generation tag (never 0)
     int* status;
+};
+
+constexpr int kMinTilesPerCta = 8;  // small problems use fewer CTAs, hence fewer pieces
+
+// The CTA's slice of the flat tile list, computed once by the producer warp.
+struct Sched {
+    int s, h, j, tiles, len, seq;  // cursor at the first tile
+    int count;                     // tiles in this CTA's range
+    int g_first;                   // global index of the first tile
+    int total;                     // tiles over all segments
+    int n_eff;                     // CTAs that received work
 };
 
 template <int ROWS>
@@ -70,8 +75,8 @@ struct DecodeSmem {
     float merge_l[kDecConsumerWarps][ROWS];
     uint64_t full[kDecStages];
     uint64_t empty[kDecStages];
-    long long sched[6];        // first seq index, kv head, tile, tile count, first tile, total
-    int flag;                  // piece-combine broadcast
+    Sched sched;
+    int cstart[kMaxPieces];    // first global tile of CTA c, c in [0, n_eff]
 };
 
 __device__ __forceinline__ int tiles_of(int len) { return (len + kBlockTokens - 1) / kBlockTokens; }
@@ -103,65 +108,85 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p)
     while (c.tiles == 0 && s < p.n_seqs) cursor_load(c, p, ++s);
 }
 
-// Warp-wide computation of the CTA's range: returns total tiles T and fills
-// the starting cursor / count.  All lanes of the calling warp participate.
-__device__ long long locate_range(const DecodeParams& p, int cta, int n_ctas, Cursor& cur,
-                                  long long& count)
+// Producer-warp planning, all lanes: total tiles T, the number of CTAs that
+// get work (n_eff = min(grid, ceil(T / kMinTilesPerCta))), every CTA's first
+// tile (cstart, so later piece arithmetic is a shared-memory lookup), and
+// this CTA's starting cursor.
+template <int ROWS>
+__device__ void plan_cta(const DecodeParams& p, int cta, int grid, DecodeSmem<ROWS>& sm)
 {
     const int lane = threadIdx.x & 31;
     const int hkv = p.view.hkv;
     long long total = 0;
     for (int base = 0; base < p.n_seqs; base += 32) {
-        int s = base + lane;
+        const int s = base + lane;
         int t = s < p.n_seqs ? tiles_of(clamp_len(p.lengths[s], p.view.capacity)) : 0;
 #pragma unroll
         for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
         total += t;
     }
     total *= hkv;
-    const long long g0 = total * cta / n_ctas, g1 = total * (cta + 1) / n_ctas;
-    count = g1 - g0;
-    cur.s = p.n_seqs;
-    cur.h = cur.j = 0;
-    if (count <= 0) return total;
-    long long run = 0;  // tiles before the current chunk
-    for (int base = 0; base < p.n_seqs; base += 32) {
-        int s = base + lane;
-        long long t = s < p.n_seqs ? (long long)tiles_of(clamp_len(p.lengths[s], p.view.capacity)) * hkv : 0;
-        long long incl = t;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            long long y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        unsigned hit = __ballot_sync(0xffffffffu, run + incl > g0);
-        if (hit) {
-            int src = __ffs(hit) - 1;
-            long long before = run + __shfl_sync(0xffffffffu, incl - t, src);
-            int s_hit = base + src;
-            cursor_load(cur, p, s_hit);
-            long long off = g0 - before;
-            cur.h = (int)(off / cur.tiles);
-            cur.j = (int)(off % cur.tiles);
-            return total;
-        }
-        run += __shfl_sync(0xffffffffu, incl, 31);
+    if (total >= (1ll << 31) / kMaxPieces) {
+        // the int tile arithmetic below would overflow: refuse the work
+        if (lane == 0) record_status(p.status, HX_ERR_CAPACITY);
+        total = 0;
     }
-    return total;
+    const int T = (int)total;
+    const int want = (T + kMinTilesPerCta - 1) / kMinTilesPerCta;
+    const int n_eff = max(1, min(grid, want));
+    for (int c = lane; c <= n_eff; c += 32) sm.cstart[c] = (int)((long long)T * c / n_eff);
+    __syncwarp();
+    Sched sc{};
+    sc.total = T;
+    sc.n_eff = n_eff;
+    sc.s = p.n_seqs;
+    if (cta < n_eff) {
+        sc.g_first = sm.cstart[cta];
+        sc.count = sm.cstart[cta + 1] - sc.g_first;
+    }
+    if (sc.count > 0) {
+        const int g0 = sc.g_first;
+        int run = 0;  // tiles before the current chunk
+        for (int base = 0; base < p.n_seqs; base += 32) {
+            const int s = base + lane;
+            const int t = s < p.n_seqs ? tiles_of(clamp_len(p.lengths[s], p.view.capacity)) * hkv : 0;
+            int incl = t;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, run + incl > g0);
+            if (hit) {
+                const int src = __ffs(hit) - 1;
+                const int before = run + __shfl_sync(0xffffffffu, incl - t, src);
+                Cursor c{};
+                cursor_load(c, p, base + src);
+                const int off = g0 - before;
+                sc.s = c.s;
+                sc.len = c.len;
+                sc.tiles = c.tiles;
+                sc.seq = c.seq;
+                sc.h = off / c.tiles;
+                sc.j = off % c.tiles;
+                break;
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+    if (lane == 0) sm.sched = sc;
 }
 
-__device__ __forceinline__ long long cta_start(long long c, long long total, int n_ctas)
+// The CTA whose non-empty range [cstart[c], cstart[c+1]) holds global tile g.
+__device__ __forceinline__ int cta_of_tile(const int* cstart, int n_eff, int g)
 {
-    return total * c / n_ctas;
-}
-
-// The CTA whose tile range [start(c), start(c+1)) holds global tile g.
-__device__ __forceinline__ int cta_of_tile(long long g, long long total, int n_ctas)
-{
-    long long c = g * n_ctas / total;
-    while (c + 1 < n_ctas && cta_start(c + 1, total, n_ctas) <= g) ++c;
-    while (c > 0 && cta_start(c, total, n_ctas) > g) --c;
-    return (int)c;
+    int lo = 0, hi = n_eff - 1;
+    while (lo < hi) {  // largest c with cstart[c] <= g
+        const int mid = (lo + hi + 1) >> 1;
+        if (cstart[mid] <= g) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
 }
 
 __device__ __forceinline__ void store_out(const DecodeParams& p, int s, int h, int r, int d, float val)
@@ -171,102 +196,6 @@ __device__ __forceinline__ void store_out(const DecodeParams& p, int s, int h, i
         static_cast<float*>(p.out)[oi] = val;
     else
         static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
-}
-
-// Counts this piece in the segment's ticket and returns the pieces seen so
-// far in this call.  A ticket holding another generation is stale (an
-// earlier call, or fresh memory) and restarts at one.
-__device__ __forceinline__ uint32_t ticket_arrive(unsigned long long* t, uint32_t gen)
-{
-    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(t), seen;
-    do {
-        seen = old;
-        const unsigned long long cnt = (uint32_t)(seen >> 32) == gen ? (seen & 0xffffffffull) : 0ull;
-        old = atomicCAS(t, seen, ((unsigned long long)gen << 32) | (cnt + 1));
-    } while (old != seen);
-    const unsigned long long cnt = (uint32_t)(seen >> 32) == gen ? (seen & 0xffffffffull) : 0ull;
-    return (uint32_t)(cnt + 1);
-}
-
-// Log-sum-exp merge of every piece of segment (s, h) by the 128 consumer
-// threads.  Pieces: slot `seg` (the one starting at the segment's first tile),
-// then slot n_seg + c for each CTA c whose non-empty range starts inside the
-// segment, in increasing c (at most C + 1 <= kMaxPieces pieces).  Step 1: each
-// warp takes rows r = warp (mod 4) and spreads the pieces over its lanes to get
-// the row's max and normaliser; the normalised per-piece weights go to shared
-// memory.  Step 2, per row: thread (q, d4) sums every fourth piece for dims
-// 4*d4..4*d4+3 with float4 loads, 8 in flight, and the four partial sums meet
-// in shared memory.  `scratch` (the merge buffer, 4*ROWS*128 floats) holds
-// the slot list, the weights and the partial sums:
-// kMaxPieces + ROWS*kMaxPieces + 512 floats.
-template <int ROWS>
-__device__ void combine_segment(const DecodeParams& p, int seg, int s, int h, int c_first,
-                                int c_last, long long total, int n_ctas, int n_seg, float* scratch)
-{
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    int* slot_list = reinterpret_cast<int*>(scratch);
-    float* weights = scratch + kMaxPieces;
-    static_assert(kMaxPieces + ROWS * kMaxPieces + 512 <= kDecConsumerWarps * ROWS * 128,
-                  "combine scratch exceeds the merge buffer");
-    float4* partial = reinterpret_cast<float4*>(scratch + kMaxPieces + ROWS * kMaxPieces);
-    if (t == 0) {
-        int np = 0;
-        slot_list[np++] = seg;
-        for (int c = c_first + 1; c <= c_last && np < kMaxPieces - 1; ++c)
-            if (cta_start(c + 1, total, n_ctas) > cta_start(c, total, n_ctas)) slot_list[np++] = n_seg + c;
-        slot_list[kMaxPieces - 1] = np;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-    const int np = slot_list[kMaxPieces - 1];
-    for (int r = warp; r < p.group; r += kDecConsumerWarps) {
-        float M = -INFINITY;
-        for (int q = lane; q < np; q += 32)
-            M = fmaxf(M, __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r].x));
-#pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f;
-        for (int q = lane; q < np; q += 32) {
-            const float2 ml = __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r]);
-            const float w = fast_exp2(ml.x - Mu);
-            weights[r * kMaxPieces + q] = w;
-            L += w * ml.y;
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float inv = 1.f / L;
-        __syncwarp();
-        for (int q = lane; q < np; q += 32) weights[r * kMaxPieces + q] *= inv;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-    const int d4 = lane, qoff = warp;
-    for (int r = 0; r < p.group; ++r) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q0 = qoff; q0 < np; q0 += 4 * 8) {
-            float4 v[8];
-            float w[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int q = q0 + 4 * u;
-                w[u] = q < np ? weights[r * kMaxPieces + q] : 0.f;
-                v[u] = q < np ? __ldcg(reinterpret_cast<const float4*>(
-                                    p.ws_o + ((int64_t)slot_list[q] * p.group + r) * 128) + d4)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                acc.x += w[u] * v[u].x;
-                acc.y += w[u] * v[u].y;
-                acc.z += w[u] * v[u].z;
-                acc.w += w[u] * v[u].w;
-            }
-        }
-        partial[qoff * 32 + d4] = acc;
-        asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-        const float* pf = reinterpret_cast<const float*>(partial);
-        store_out(p, s, h, r, t, pf[t] + pf[128 + t] + pf[256 + t] + pf[384 + t]);
-        asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-    }
 }
 
 // Sequences with no positions attend to nothing: their rows are zeros.
@@ -298,6 +227,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int cta = blockIdx.x, n_ctas = gridDim.x;
     const int n_seg = p.n_seqs * p.view.hkv;
 
+    // With HX_KV_OVERLAP_LAUNCH this kernel may start before the previous one
+    // on the stream (normally hx_rope_append) has finished.  Until pdl_wait()
+    // it reads only lengths, seq_ids, the block table and cache positions
+    // below each sequence's newest one; q, the newest position and every write
+    // come after it.
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecStages; ++i) {
             mbar_init(&sm.full[i], 1);
@@ -305,28 +240,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         fence_mbar_init();
     }
-    if (warp == kDecConsumerWarps) {
-        Cursor c{};
-        long long count = 0;
-        const long long total = locate_range(p, cta, n_ctas, c, count);
-        if (lane == 0) {
-            sm.sched[0] = c.s;
-            sm.sched[1] = c.h;
-            sm.sched[2] = c.j;
-            sm.sched[3] = count;
-            sm.sched[4] = total * cta / n_ctas;
-            sm.sched[5] = total;
-        }
-        if (cta == 0) zero_empty_outputs(p);
-    }
+    if (warp == kDecConsumerWarps) plan_cta(p, cta, n_ctas, sm);
     __syncthreads();
-    const long long count = sm.sched[3];
-    const long long g_first = sm.sched[4], total_tiles = sm.sched[5];
+    const Sched sc = sm.sched;
+    const int count = sc.count;
+    if (cta == 0 && warp == 0) {
+        pdl_wait();
+        zero_empty_outputs(p);
+    }
     if (count <= 0) return;
-    Cursor cur{};
-    cursor_load(cur, p, (int)sm.sched[0]);
-    cur.h = (int)sm.sched[1];
-    cur.j = (int)sm.sched[2];
+    const int g_first = sc.g_first, n_eff = sc.n_eff;
+    Cursor cur{sc.s, sc.h, sc.j, sc.tiles, sc.len, sc.seq};
 
     if (warp == kDecConsumerWarps) {
         // ------------------------------------------------------------ producer
@@ -335,12 +259,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         prefetch_tensormap(&tm_v);
         const uint64_t pol = l2_evict_first_policy();
         const KVView& v = p.view;
-        for (long long i = 0; i < count; ++i) {
-            const int st = (int)(i % kDecStages);
+        bool waited = false;
+        for (int i = 0; i < count; ++i) {
+            const int st = i % kDecStages;
             const uint32_t round = (uint32_t)(i / kDecStages);
             if (i >= kDecStages && !mbar_wait(&sm.empty[st], (round - 1) & 1)) {
                 record_status(p.status, HX_ERR_TIMEOUT);
                 return;
+            }
+            if (!waited && cur.j == cur.tiles - 1) {
+                pdl_wait();  // the segment's last tile holds the newest position
+                waited = true;
             }
             const int64_t pb = phys_block(v, cur.seq, cur.j);
             if (pb < 0) {
@@ -362,8 +291,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             cursor_next(cur, p);
         }
         // Wait for the last copies to land before the CTA may exit.
-        for (long long i = count > kDecStages ? count - kDecStages : 0; i < count; ++i) {
-            const int st = (int)(i % kDecStages);
+        for (int i = count > kDecStages ? count - kDecStages : 0; i < count; ++i) {
+            const int st = i % kDecStages;
             if (!mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1)) {
                 record_status(p.status, HX_ERR_TIMEOUT);
                 return;
@@ -373,6 +302,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
 
     // ---------------------------------------------------------------- consumers
+    pdl_wait();  // q and the newest cache position come from the previous kernel
     const int g = lane >> 2, t4 = lane & 3;
     const int w = warp;
     uint32_t qa[8][4];
@@ -383,7 +313,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // ldmatrix row addresses (before swizzle) for this lane
     const int lm_mi = lane >> 3, lm_r = lane & 7;
 
-    for (long long i = 0; i < count; ++i) {
+    for (int i = 0; i < count; ++i) {
         if (i == 0 || cur.j == 0) {
             // new piece: load the packed GQA group of q rows for (s, h)
             piece_from_seg_start = (cur.j == 0);
@@ -417,7 +347,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             l0 = l1 = 0.f;
         }
 
-        const int st = (int)(i % kDecStages);
+        const int st = i % kDecStages;
         if (!mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1)) {
             record_status(p.status, HX_ERR_TIMEOUT);
             return;
@@ -568,9 +498,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
             const int d = threadIdx.x;  // 0..127
             // global tile range [a, b) of this segment and the CTAs that share it
-            const long long a = g_first + i - cur.j, b = a + cur.tiles;
-            const int c_first = cta_of_tile(a, total_tiles, n_ctas);
-            const int c_last = cta_of_tile(b - 1, total_tiles, n_ctas);
+            const int a = g_first + i - cur.j, b = a + cur.tiles;
+            const int c_first = cta_of_tile(sm.cstart, n_eff, a);
+            const int c_last = cta_of_tile(sm.cstart, n_eff, b - 1);
             const bool whole = c_first == c_last;
             const int seg = cur.s * p.view.hkv + cur.h;
             const int slot = piece_from_seg_start ? seg : (n_seg + cta);
@@ -593,28 +523,123 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
                 }
             }
-            if (!whole) {
-                // Publish this piece; the CTA whose piece completes the
-                // segment merges all of them (fixed order: deterministic).
-                __threadfence();
-                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-                if (d == 0) {
-                    int n_pieces = 0;
-                    for (int c = c_first; c <= c_last; ++c)
-                        n_pieces += cta_start(c + 1, total_tiles, n_ctas) > cta_start(c, total_tiles, n_ctas);
-                    sm.flag = ticket_arrive(p.tickets + seg, p.gen) == (uint32_t)n_pieces;
-                }
-                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-                if (sm.flag) {
-                    __threadfence();
-                    combine_segment<ROWS>(p, seg, cur.s, cur.h, c_first, c_last, total_tiles, n_ctas,
-                                    n_seg, &sm.merge_o[0][0][0]);
-                }
-            }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
         }
         cursor_next(cur, p);
     }
+}
+
+// Split-K combine: one CTA (128 threads, one per dim) per (segment, q row of
+// the group), launched right after the decode kernel as a programmatic
+// dependent, so it is resident early and starts as soon as the decode grid
+// has finished.  Segments that one CTA covered were already written by the
+// decode kernel.  The pieces are slot `seg` (the one starting at the
+// segment's first tile) then slot n_seg + c for each CTA c whose non-empty
+// range starts inside the segment, merged in that fixed order: warp 0 loads
+// every piece's (m, l) in one round and leaves normalised weights in shared
+// memory; each thread then loads its dim of every piece in one round.
+__global__ void __launch_bounds__(128)
+    decode_combine_kernel(const DecodeParams p, int grid_ctas)
+{
+    pdl_trigger();
+    const int seg = blockIdx.x, r = blockIdx.y;
+    const int hkv = p.view.hkv;
+    const int s = seg / hkv, h = seg % hkv;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    __shared__ int sh_range[4];  // a, b, T, n_eff
+    __shared__ int slot_list[kMaxPieces];
+    __shared__ float weights[kMaxPieces];
+    __shared__ int sh_np;
+    if (warp == 0) {
+        int before = 0, total = 0;
+        for (int base = 0; base < p.n_seqs; base += 32) {
+            const int si = base + lane;
+            int tl = si < p.n_seqs ? tiles_of(clamp_len(p.lengths[si], p.view.capacity)) : 0;
+            int tb = si < s ? tl : 0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                tl += __shfl_xor_sync(0xffffffffu, tl, o);
+                tb += __shfl_xor_sync(0xffffffffu, tb, o);
+            }
+            total += tl;
+            before += tb;
+        }
+        if (lane == 0) {
+            const int tiles = tiles_of(clamp_len(p.lengths[s], p.view.capacity));
+            const long long T = (long long)total * hkv;
+            const int valid_T = T < (1ll << 31) / kMaxPieces ? (int)T : 0;
+            const int n_eff = max(1, min(grid_ctas, (valid_T + kMinTilesPerCta - 1) / kMinTilesPerCta));
+            sh_range[0] = before * hkv + h * tiles;
+            sh_range[1] = sh_range[0] + tiles;
+            sh_range[2] = valid_T;
+            sh_range[3] = n_eff;
+        }
+    }
+    __syncthreads();
+    const int a = sh_range[0], b = sh_range[1], T = sh_range[2], n_eff = sh_range[3];
+    if (a >= b || T == 0) return;
+    auto cstart = [&](int c) { return (int)((long long)T * c / n_eff); };
+    if (t == 0) {
+        int c = (int)((long long)a * n_eff / T);
+        while (c + 1 < n_eff && cstart(c + 1) <= a) ++c;
+        while (c > 0 && cstart(c) > a) --c;
+        int np = 0;
+        slot_list[np++] = seg;
+        const int n_seg = p.n_seqs * hkv;
+        for (int cc = c + 1; cc < n_eff && cstart(cc) < b && np < kMaxPieces; ++cc)
+            if (cstart(cc + 1) > cstart(cc)) slot_list[np++] = n_seg + cc;
+        sh_np = np;
+    }
+    __syncthreads();
+    const int np = sh_np;
+    if (np <= 1) return;  // one piece: the decode kernel wrote the output
+    pdl_wait();           // the pieces come from the decode grid
+    if (warp == 0) {
+        constexpr int kPerLane = (kMaxPieces + 31) / 32;
+        float2 ml[kPerLane];
+#pragma unroll
+        for (int u = 0; u < kPerLane; ++u) {
+            const int q = lane + 32 * u;
+            ml[u] = q < np ? __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r])
+                           : make_float2(-INFINITY, 0.f);
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kPerLane; ++u) M = fmaxf(M, ml[u].x);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, w[kPerLane];
+#pragma unroll
+        for (int u = 0; u < kPerLane; ++u) {
+            w[u] = fast_exp2(ml[u].x - Mu);
+            L += w[u] * ml[u].y;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = 1.f / L;
+#pragma unroll
+        for (int u = 0; u < kPerLane; ++u) {
+            const int q = lane + 32 * u;
+            if (q < np) weights[q] = w[u] * inv;
+        }
+    }
+    // each thread's loads do not depend on the weights: issue them first
+    constexpr int kBatch = 32;
+    float acc = 0.f;
+    for (int q0 = 0; q0 < np; q0 += kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int q = q0 + u;
+            v[u] = q < np ? __ldcg(p.ws_o + ((int64_t)slot_list[q] * p.group + r) * 128 + t) : 0.f;
+        }
+        __syncthreads();  // weights ready (first batch); harmless afterwards
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (q0 + u < np) acc += weights[q0 + u] * v[u];
+    }
+    store_out(p, s, h, r, t, acc);
 }
 
 // Any head_dim (<= 256), any group: one CTA of 4 warps per (sequence, q
@@ -698,11 +723,10 @@ __global__ void __launch_bounds__(128)
 static size_t decode_ws_bytes(int n_seqs, int hkv, int group, int n_ctas)
 {
     const size_t slots = (size_t)n_seqs * hkv + n_ctas;
-    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2) +
-           (size_t)n_seqs * hkv * sizeof(unsigned long long);
+    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2);
 }
 
-// Layout of the workspace: [ws_o][ws_ml][tickets].
+// Layout of the workspace: [ws_o][ws_ml].
 static void bind_workspace(DecodeParams& p, void* ws, int n_ctas)
 {
     const size_t slots = (size_t)p.n_seqs * p.view.hkv + n_ctas;
@@ -710,18 +734,9 @@ static void bind_workspace(DecodeParams& p, void* ws, int n_ctas)
     p.ws_o = reinterpret_cast<float*>(base);
     base += slots * p.group * 128 * sizeof(float);
     p.ws_ml = reinterpret_cast<float2*>(base);
-    base += slots * p.group * sizeof(float2);
-    p.tickets = reinterpret_cast<unsigned long long*>(base);
 }
 
-static std::atomic<uint32_t> g_generation{0};
 
-static uint32_t next_generation()
-{
-    uint32_t g = ++g_generation;
-    if (g == 0) g = ++g_generation;
-    return g;
-}
 
 template <int ROWS>
 static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas,
@@ -736,8 +751,15 @@ static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr_set[dev] = true;
     }
-    decode_attention_kernel<ROWS><<<n_ctas, kDecThreads, smem, stream>>>(c->tm_k, c->tm_v, p);
-    return check_launch("decode_attention_kernel");
+    const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
+    cudaError_t e = launch_kernel(decode_attention_kernel<ROWS>, dim3(n_ctas), dim3(kDecThreads),
+                                  smem, stream, ov, c->tm_k, c->tm_v, p);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attention_kernel launch");
+    if (int rc = check_launch("decode_attention_kernel")) return rc;
+    e = launch_kernel(decode_combine_kernel, dim3(p.n_seqs * p.view.hkv, p.group), dim3(128), 0,
+                      stream, true, p, n_ctas);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_combine_kernel launch");
+    return check_launch("decode_combine_kernel");
 }
 
 }  // namespace hx
@@ -794,7 +816,6 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
         return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
                     workspace_bytes, need);
     bind_workspace(p, workspace, n_ctas);
-    p.gen = next_generation();
     if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
     return launch_decode<16>(c, p, n_ctas, s);
 }
@@ -817,11 +838,9 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
 // first call on a device should therefore happen before any stream capture.
 //
 // All calls share the array and it keeps the last call's contents: the decode
-// kernel writes every slot its combine step reads within the same call, and
-// the per-segment tickets carry a per-call generation tag (a ticket from an
-// earlier call restarts at one), so nothing needs clearing; but two calls
-// that overlap on the GPU (different streams, devices aside) race on the
-// scratch.  Kernel-side faults of this
+// kernel writes every slot its combine step reads within the same call, so
+// nothing needs clearing; but two calls that overlap on the GPU (different
+// streams, devices aside) race on the scratch.  Kernel-side faults of this
 // entry point are not recorded in the device status word (setting that word
 // up may allocate); bounds are still checked and waits still bounded.
 namespace hx {
@@ -890,7 +909,6 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
         return check_launch("decode_generic_kernel");
     }
     bind_workspace(p, scratch, n_ctas);
-    p.gen = next_generation();
     if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
     return launch_decode<16>(c, p, n_ctas, s);
 }

@@ -158,8 +158,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     auto& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // longest tiles first
-    const int h = blockIdx.y, kvh = h / p.group;
+    // grid (q heads, query tiles): the last query tiles (most key tiles)
+    // of every head are issued first
+    const int qt = p.n_qtiles - 1 - (int)blockIdx.y;
+    const int h = blockIdx.x, kvh = h / p.group;
     const int q0 = qt * 128;
     const int rows_valid = min(128, p.n - q0);
     const int kend = p.start + q0 + rows_valid;  // keys [0, kend) are needed by this tile
@@ -479,7 +481,7 @@ extern "C" int hx_prefill_attention(const hx_kv_cache* c, int layer, const void*
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr_set[dev] = true;
     }
-    dim3 grid(p.n_qtiles, num_q_heads);
+    dim3 grid(num_q_heads, p.n_qtiles);
     prefill_attention_kernel<<<grid, kPfThreads, smem, (cudaStream_t)stream>>>(tm_q, c->tm_k, c->tm_v, p);
     return check_launch("prefill_attention_kernel");
 }

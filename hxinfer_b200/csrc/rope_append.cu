@@ -55,9 +55,10 @@ __device__ __forceinline__ void rotate(float x1, float x2, float2 cs, float& o1,
     o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
 }
 
-// One block per token.  Work items (slot, d): slot in [0, hq) = q heads,
-// [hq, hq+hkv) = k heads, [hq+hkv, hq+2hkv) = v heads; item d < head_dim/2
-// handles the NeoX pair (d, d + head_dim/2).
+// grid (token, head group): each CTA takes heads_per_cta consecutive head
+// slots of one token, one thread per NeoX pair (d, d + head_dim/2), so every
+// load of a token's step is issued at once.  Slots: [0, hq) = q heads,
+// [hq, hq+hkv) = k heads, [hq+hkv, hq+2hkv) = v heads.
 template <typename T, typename TO>
 __global__ void rope_append_kernel(KVView view, const T* __restrict__ q, const T* __restrict__ k,
                                    const T* __restrict__ v, const T* __restrict__ bq,
@@ -65,48 +66,49 @@ __global__ void rope_append_kernel(KVView view, const T* __restrict__ q, const T
                                    const int32_t* __restrict__ seq_ids,
                                    const int32_t* __restrict__ positions, int hq,
                                    const float2* __restrict__ table, int table_max_pos,
-                                   TO* __restrict__ q_out, int* status)
+                                   TO* __restrict__ q_out, int heads_per_cta, int* status)
 {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the previous kernel on the stream
     const int i = blockIdx.x;
     const int hd = view.hd, half = hd / 2, hkv = view.hkv;
+    const int q_heads = q ? hq : 0;
+    const int slot = blockIdx.y * heads_per_cta + (int)threadIdx.x / half;
+    const int d = (int)threadIdx.x % half;
+    if ((int)threadIdx.x >= heads_per_cta * half || slot >= q_heads + 2 * hkv) return;
     const int seq = seq_ids[i], pos = positions[i];
     if (seq < 0 || seq >= view.max_seqs || pos < 0 || pos >= view.capacity ||
         (table && pos >= table_max_pos)) {
         if (threadIdx.x == 0) record_status(status, HX_ERR_CAPACITY);
         return;
     }
-    const int q_heads = q ? hq : 0;
-    const int items = (q_heads + 2 * hkv) * half;
     const float2* cs_row = table ? table + (int64_t)pos * half : nullptr;
-    for (int it = threadIdx.x; it < items; it += blockDim.x) {
-        const int slot = it / half, d = it % half;
-        if (slot < q_heads) {
-            const int64_t base = ((int64_t)i * hq + slot) * hd + d;
-            const T* b = bq ? bq + (int64_t)slot * hd + d : nullptr;
-            float x1 = ld_bias(q + base, b), x2 = ld_bias(q + base + half, b ? b + half : nullptr);
-            if (cs_row) rotate(x1, x2, cs_row[d], x1, x2);
-            if (q_out) {
-                st(q_out + base, x1);
-                st(q_out + base + half, x2);
-            }
-            continue;
+    if (slot < q_heads) {
+        const int64_t base = ((int64_t)i * hq + slot) * hd + d;
+        const T* b = bq ? bq + (int64_t)slot * hd + d : nullptr;
+        float x1 = ld_bias(q + base, b), x2 = ld_bias(q + base + half, b ? b + half : nullptr);
+        if (cs_row) rotate(x1, x2, cs_row[d], x1, x2);
+        if (q_out) {
+            st(q_out + base, x1);
+            st(q_out + base + half, x2);
         }
-        const bool is_k = slot < q_heads + hkv;
-        const int h = is_k ? slot - q_heads : slot - q_heads - hkv;
-        const T* src = (is_k ? k : v) + ((int64_t)i * hkv + h) * hd + d;
-        const T* bias = is_k ? bk : bv;
-        const T* b = bias ? bias + (int64_t)h * hd + d : nullptr;
-        float x1 = ld_bias(src, b), x2 = ld_bias(src + half, b ? b + half : nullptr);
-        if (is_k && cs_row) rotate(x1, x2, cs_row[d], x1, x2);
-        const int64_t off = token_offset(view, seq, h, pos);
-        if (off < 0) {
-            record_status(status, HX_ERR_CAPACITY);
-            continue;
-        }
-        __half* dst = reinterpret_cast<__half*>((is_k ? view.k : view.v) + off);
-        dst[d] = __float2half_rn(x1);
-        dst[d + half] = __float2half_rn(x2);
+        return;
     }
+    const bool is_k = slot < q_heads + hkv;
+    const int h = is_k ? slot - q_heads : slot - q_heads - hkv;
+    const T* src = (is_k ? k : v) + ((int64_t)i * hkv + h) * hd + d;
+    const T* bias = is_k ? bk : bv;
+    const T* b = bias ? bias + (int64_t)h * hd + d : nullptr;
+    float x1 = ld_bias(src, b), x2 = ld_bias(src + half, b ? b + half : nullptr);
+    if (is_k && cs_row) rotate(x1, x2, cs_row[d], x1, x2);
+    const int64_t off = token_offset(view, seq, h, pos);
+    if (off < 0) {
+        record_status(status, HX_ERR_CAPACITY);
+        return;
+    }
+    __half* dst = reinterpret_cast<__half*>((is_k ? view.k : view.v) + off);
+    dst[d] = __float2half_rn(x1);
+    dst[d + half] = __float2half_rn(x2);
 }
 
 // In-place RoPE of q [rows][hq*hd] and k [rows][hkv*hd] at one position.
@@ -157,32 +159,37 @@ extern "C" int hx_rope_append(hx_kv_cache* c, int layer, const void* q, const vo
     KVView view = make_view(c, layer);
     const float2* tab = table ? table->d_cos_sin : nullptr;
     const int tmax = table ? table->cfg.max_pos : 0;
+    const int half = hd / 2;
     const int threads = 256;
+    const int heads_per_cta = std::max(1, threads / half);
+    const int slots = (q ? num_q_heads : 0) + 2 * c->cfg.num_kv_heads;
+    const dim3 grid(n_tokens, (slots + heads_per_cta - 1) / heads_per_cta);
     cudaStream_t s = (cudaStream_t)stream;
     int* sw = status_word();
+    const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
     const bool q16 = !q_out || q_out_dtype == HX_FP16;
     if (dtype == HX_FP16) {
         if (q16)
-            rope_append_kernel<__half, __half><<<n_tokens, threads, 0, s>>>(
+            launch_kernel(rope_append_kernel<__half, __half>, grid, dim3(threads), 0, s, ov,
                 view, (const __half*)q, (const __half*)k, (const __half*)v, (const __half*)bq,
                 (const __half*)bk, (const __half*)bv, seq_ids, positions, num_q_heads, tab, tmax,
-                (__half*)q_out, sw);
+                (__half*)q_out, heads_per_cta, sw);
         else
-            rope_append_kernel<__half, float><<<n_tokens, threads, 0, s>>>(
+            launch_kernel(rope_append_kernel<__half, float>, grid, dim3(threads), 0, s, ov,
                 view, (const __half*)q, (const __half*)k, (const __half*)v, (const __half*)bq,
                 (const __half*)bk, (const __half*)bv, seq_ids, positions, num_q_heads, tab, tmax,
-                (float*)q_out, sw);
+                (float*)q_out, heads_per_cta, sw);
     } else {
         if (q16)
-            rope_append_kernel<float, __half><<<n_tokens, threads, 0, s>>>(
+            launch_kernel(rope_append_kernel<float, __half>, grid, dim3(threads), 0, s, ov,
                 view, (const float*)q, (const float*)k, (const float*)v, (const float*)bq,
                 (const float*)bk, (const float*)bv, seq_ids, positions, num_q_heads, tab, tmax,
-                (__half*)q_out, sw);
+                (__half*)q_out, heads_per_cta, sw);
         else
-            rope_append_kernel<float, float><<<n_tokens, threads, 0, s>>>(
+            launch_kernel(rope_append_kernel<float, float>, grid, dim3(threads), 0, s, ov,
                 view, (const float*)q, (const float*)k, (const float*)v, (const float*)bq,
                 (const float*)bk, (const float*)bv, seq_ids, positions, num_q_heads, tab, tmax,
-                (float*)q_out, sw);
+                (float*)q_out, heads_per_cta, sw);
     }
     return check_launch("rope_append_kernel");
 }

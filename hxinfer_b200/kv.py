@@ -93,7 +93,8 @@ class KVCache:
     """Paged head-major fp16 KV cache for every layer of a model (or a shard)."""
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_seqs: int,
-                 max_tokens_per_seq: int, num_blocks: int = 0, *, _handle=None):
+                 max_tokens_per_seq: int, num_blocks: int = 0, *, overlap: bool = False,
+                 _handle=None):
         self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
         self.max_seqs, self.max_tokens_per_seq = max_seqs, max_tokens_per_seq
         if _handle is not None:
@@ -101,7 +102,8 @@ class KVCache:
             return
         cfg = _lib.hx_kv_config(num_layers=num_layers, num_kv_heads=num_kv_heads,
                                 head_dim=head_dim, max_seqs=max_seqs,
-                                max_tokens_per_seq=max_tokens_per_seq, num_blocks=num_blocks)
+                                max_tokens_per_seq=max_tokens_per_seq, num_blocks=num_blocks,
+                                flags=_lib.HX_KV_OVERLAP_LAUNCH if overlap else 0)
         h = C.c_void_p()
         check(load().hx_kv_create(C.byref(cfg), C.byref(h)), "kv create")
         self.handle = h
@@ -188,7 +190,7 @@ class KVCache:
             out = torch.empty((n, num_q_heads * self.head_dim), dtype=out_dtype, device=q.device)
         ws_need = self.workspace_bytes(n, num_q_heads)
         if workspace is None:
-            workspace = torch.empty(max(ws_need, 16), dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(max(ws_need, 16), dtype=torch.uint8, device=q.device)
         check(load().hx_decode_attention(self.handle, layer, _ptr(q), _dt(q), _ptr(seq_ids),
                                          _ptr(lengths), n, num_q_heads, scale, _ptr(out), _dt(out),
                                          _ptr(workspace), workspace.numel() * workspace.element_size(),

@@ -25,10 +25,13 @@ SHAPES = {"llama3": (32, 8, 5e5), "qwen": (28, 4, 1e6), "llama2": (32, 32, 1e4)}
 
 
 def decode_case(a):
+    """Decode steps over `layers` layers, timed as CUDA-graph replays (so the
+    host's launch rate does not limit small cases): per layer the fused
+    RoPE+append (K1) then the split-K decode (K2); also K2 alone."""
     hq, hkv, theta = SHAPES[a.shape]
     hd, n, L, layers = 128, a.seqs, a.len, a.layers
-    cap = L + a.iters + 2
-    cache = kv.KVCache(layers, hkv, hd, n, cap)
+    cap = L + 2
+    cache = kv.KVCache(layers, hkv, hd, n, cap, overlap=a.overlap)
     for s in range(n):
         cache.reserve(s, cap)
     cache.fill_normal(7)
@@ -41,28 +44,43 @@ def decode_case(a):
     q_rot = torch.empty_like(q)
     out = torch.empty_like(q)
     sid = torch.arange(n, dtype=torch.int32, device="cuda")
-    ws = torch.empty(cache.workspace_bytes(n, hq), dtype=torch.uint8, device="cuda")
-    evs = []
-    for it in range(a.iters):
-        pos = torch.full((n,), L - 1 + it, dtype=torch.int32, device="cuda")
-        lens = pos + 1
+    ws = torch.zeros(cache.workspace_bytes(n, hq), dtype=torch.uint8, device="cuda")
+    pos = torch.full((n,), L - 1, dtype=torch.int32, device="cuda")
+    lens = pos + 1
+    stream = torch.cuda.Stream()
+
+    def step(with_append):
         for l in range(layers):
-            cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
-                              q_out=q_rot[l])
+            if with_append:
+                cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
+                                  q_out=q_rot[l], stream=stream)
+            cache.decode(l, q_rot[l], sid, lens, hq, out=out[l], workspace=ws, stream=stream)
+
+    res = {}
+    with torch.cuda.stream(stream):
+        step(True)  # warm-up (sets kernel attributes outside capture)
+        torch.cuda.synchronize()
+        for name, app in (("step", True), ("decode_only", False)):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(app)
+            graph.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            cache.decode(l, q_rot[l], sid, lens, hq, out=out[l], workspace=ws)
-            e1.record()
-            evs.append((e0, e1))
-    torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(a.iters):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            res[name] = e0.elapsed_time(e1) / (a.iters * layers)
     kv.device_status()
-    skip = min(len(evs) - 1, layers)  # first iteration is warm-up
-    ms = [x.elapsed_time(y) for x, y in evs[skip:]]
-    avg = sum(ms) / len(ms)
-    nbytes = 2 * n * (L + a.iters // 2) * hkv * hd * 2
+    nbytes = 2 * n * L * hkv * hd * 2
     print(json.dumps({"case": "decode", "shape": a.shape, "seqs": n, "len": L, "layers": layers,
-                      "decode_ms_avg": avg, "bytes_per_launch": nbytes,
-                      "gbs": nbytes / (avg * 1e-3) / 1e9}))
+                      "overlap": a.overlap,
+                      "graph_us_per_layer_step": 1e3 * res["step"],
+                      "graph_us_per_layer_decode": 1e3 * res["decode_only"],
+                      "bytes_per_launch": nbytes,
+                      "decode_gbs": nbytes / (res["decode_only"] * 1e-3) / 1e9,
+                      "step_gbs": nbytes / (res["step"] * 1e-3) / 1e9}))
 
 
 def snapshot_case(a):
@@ -133,6 +151,8 @@ def main():
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--start", type=int, default=0)
+    ap.add_argument("--overlap", action="store_true",
+                    help="programmatic dependent launch of append -> decode (HX_KV_OVERLAP_LAUNCH)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case}[a.case](a)

@@ -2,7 +2,8 @@
 
 The decode kernel (csrc/decode_attention.cu) flattens every (sequence,
 kv head) segment into 64-position tiles, ordered sequence-major then kv head
-then tile, and gives CTA c of C the tiles [c*T/C, (c+1)*T/C).  The part of a
+then tile, and gives CTA c of C = min(grid, ceil(T/8)) the tiles
+[c*T/C, (c+1)*T/C).  The part of a
 segment inside one CTA is a *piece*.  A piece that starts at its segment's
 first tile stores its partial result in slot ``seq*hkv + head``; a CTA's
 first piece that starts inside a segment stores it in slot ``n_segments + c``.
@@ -16,6 +17,7 @@ combine step finds every piece, for any lengths and CTA count.
 from __future__ import annotations
 
 BLOCK = 64
+MIN_TILES_PER_CTA = 8  # the device gives each working CTA at least this many tiles
 
 
 def tiles_of(length: int) -> int:
@@ -33,6 +35,11 @@ def segment_ranges(lengths, hkv):
     return out, run
 
 
+def effective_ctas(total: int, grid: int) -> int:
+    """CTAs that receive work: min(grid, ceil(T / MIN_TILES_PER_CTA)), at least 1."""
+    return max(1, min(grid, -(-total // MIN_TILES_PER_CTA)))
+
+
 def cta_range(total: int, c: int, n_ctas: int):
     return total * c // n_ctas, total * (c + 1) // n_ctas
 
@@ -41,6 +48,7 @@ def pieces(lengths, hkv, n_ctas):
     """Pieces as written by the decode kernel: (cta, seg, first_tile, last_tile, slot, whole)."""
     segs, total = segment_ranges(lengths, hkv)
     n_seg = len(segs)
+    n_ctas = effective_ctas(total, n_ctas)
     out = []
     for c in range(n_ctas):
         g0, g1 = cta_range(total, c, n_ctas)
@@ -61,6 +69,7 @@ def combine_slots(lengths, hkv, n_ctas, seg: int):
     """Slots the combine kernel reads for `seg` ([] when one piece wrote the output)."""
     segs, total = segment_ranges(lengths, hkv)
     n_seg = len(segs)
+    n_ctas = effective_ctas(total, n_ctas)
     _, a, b = segs[seg]
     if a == b:
         return []

@@ -80,7 +80,22 @@ typedef struct {
     int32_t max_seqs;
     int32_t max_tokens_per_seq;  /* per-sequence capacity in positions */
     int64_t num_blocks;          /* physical 64-token blocks; 0 = max_seqs * ceil(max_tokens/64) */
+    int32_t flags;               /* HX_KV_* bits below; 0 = none */
 } hx_kv_config;
+
+/* hx_kv_config.flags
+ *
+ * HX_KV_OVERLAP_LAUNCH: hx_rope_append and hx_decode_attention on this cache
+ * are launched as programmatic dependents, so a launch can begin while the
+ * kernel before it on the stream is still finishing.  hx_rope_append reads
+ * nothing before that kernel has finished.  hx_decode_attention reads
+ * `lengths`, `seq_ids`, the block table and cache positions below each
+ * sequence's newest position (lengths[i] - 1) early; the kernel launched just
+ * before it on the stream must therefore write none of those -- it may write
+ * q and each sequence's newest position, which is exactly what the decode
+ * step hx_rope_append -> hx_decode_attention does.  Without the flag every
+ * launch waits for the previous kernel to finish. */
+enum { HX_KV_OVERLAP_LAUNCH = 1 };
 
 typedef struct {
     int32_t num_layers, num_kv_heads, head_dim, max_seqs, max_blocks_per_seq;
@@ -168,8 +183,9 @@ int hx_rope_append(hx_kv_cache* cache, int layer, const void* q, const void* k, 
 
 /* ------------------------------------------------------------ attention */
 
-/* Workspace bytes hx_decode_attention needs for n_seqs sequences
- * (split-K partial results; device memory owned by the caller). */
+/* Workspace bytes hx_decode_attention needs for n_seqs sequences (split-K
+ * partial results; device memory owned by the caller, no initialisation
+ * needed: every value a call reads is written by that call). */
 size_t hx_decode_workspace_bytes(const hx_kv_cache* cache, int n_seqs, int num_q_heads);
 
 /* K2: split-K GQA decode attention over the cache (replaces
@@ -177,7 +193,8 @@ size_t hx_decode_workspace_bytes(const hx_kv_cache* cache, int n_seqs, int num_q
  * q: device [n_seqs][num_q_heads*head_dim] (rotated) in q_dtype;
  * seq_ids, lengths: device int32 [n_seqs] (lengths = positions attended, >= 1);
  * out: device [n_seqs][num_q_heads*head_dim] in out_dtype.
- * q head h reads kv head h / (num_q_heads / num_kv_heads). */
+ * q head h reads kv head h / (num_q_heads / num_kv_heads).
+ * Two launches: the split-K kernel and its combine kernel. */
 int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
                         const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
                         int num_q_heads, float scale, void* out, int out_dtype, void* workspace,

@@ -222,7 +222,7 @@ def test_decode_repeated_calls_share_workspace(hx, oracle):
     q = torch.from_numpy(rng.standard_normal((3, Hq * 128)).astype(np.float16)).cuda()
     sid = torch.arange(3, dtype=torch.int32, device="cuda")
     lens = dev(np.array(lengths, np.int32))
-    ws = torch.empty(cache.workspace_bytes(3, Hq), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(cache.workspace_bytes(3, Hq), dtype=torch.uint8, device="cuda")
     outs = [cache.decode(0, q, sid, lens, Hq, workspace=ws).clone() for _ in range(3)]
     torch.cuda.synchronize()
     hx.device_status()
@@ -232,6 +232,98 @@ def test_decode_repeated_calls_share_workspace(hx, oracle):
     want = oracle.decode_attention(q[0].float().cpu().numpy(), k.reshape(lengths[0], -1).float().cpu().numpy(),
                                    v.reshape(lengths[0], -1).float().cpu().numpy(), Hq, Hkv, 128)
     assert_close(outs[0][0].float().cpu().numpy(), want, "32k after repeats")
+
+
+def test_decode_cuda_graph_replays(hx, oracle):
+    """A captured append+decode step replays correctly many times on one
+    workspace (the per-segment tickets reset themselves)."""
+    rng = np.random.default_rng(64)
+    Hq, Hkv, lengths = 28, 4, [32769, 700]
+    cache = make_cache(hx, 1, Hkv, 2, 32770)
+    for s, L in enumerate(lengths):
+        cache.reserve(s, L)
+    cache.fill_normal(65)
+    q = torch.from_numpy(rng.standard_normal((2, Hq * 128)).astype(np.float16)).cuda()
+    sid = torch.arange(2, dtype=torch.int32, device="cuda")
+    lens = dev(np.array(lengths, np.int32))
+    ws = torch.zeros(cache.workspace_bytes(2, Hq), dtype=torch.uint8, device="cuda")
+    out = torch.empty((2, Hq * 128), dtype=torch.float16, device="cuda")
+    cache.decode(0, q, sid, lens, Hq, out=out, workspace=ws)  # eager first
+    torch.cuda.synchronize()
+    want = out.clone()
+    stream = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            cache.decode(0, q, sid, lens, Hq, out=out, workspace=ws, stream=stream)
+    for _ in range(4):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+    hx.device_status()
+
+
+def _decode_steps(hx, overlap, graph, layers=4, steps=3):
+    """rope_append -> decode over `layers` layers for `steps` steps; returns
+    every step's outputs."""
+    Hq, Hkv, hd = 28, 4, 128
+    lengths = np.array([5000, 130, 64], np.int32)
+    n = len(lengths)
+    cache = hx.KVCache(layers, Hkv, hd, n, 5100, overlap=overlap)
+    for s_, L in enumerate(lengths):
+        cache.reserve(s_, int(L) + steps)
+    cache.fill_normal(99)
+    table = hx.RopeTable(hd, 5200, 1e6)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    q = torch.randn((layers, n, Hq * hd), generator=g, device="cuda").half()
+    k = torch.randn((layers, n, Hkv * hd), generator=g, device="cuda").half()
+    v = torch.randn((layers, n, Hkv * hd), generator=g, device="cuda").half()
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(cache.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda")
+    pos = torch.from_numpy(lengths).cuda()
+    lens = pos + 1
+    stream = torch.cuda.Stream()
+
+    def one_step():
+        for l in range(layers):
+            cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=Hq, table=table,
+                              q_out=q_rot[l], stream=stream)
+            cache.decode(l, q_rot[l], sid, lens, Hq, out=out[l], workspace=ws, stream=stream)
+
+    results = []
+    with torch.cuda.stream(stream):
+        if graph:
+            one_step()  # warm-up outside capture
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                one_step()
+        for _ in range(steps):
+            if graph:
+                gr.replay()
+            else:
+                one_step()
+            torch.cuda.synchronize()
+            results.append(out.clone())
+            pos += 1
+            lens += 1
+    hx.device_status()
+    return results
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_decode_overlap_launch_matches(hx, graph):
+    """HX_KV_OVERLAP_LAUNCH (programmatic dependent launch of the
+    append -> decode chain) changes timing only: outputs equal the serialised
+    launches bit for bit."""
+    a = _decode_steps(hx, overlap=False, graph=graph)
+    b = _decode_steps(hx, overlap=True, graph=graph)
+    for x, y in zip(a, b):
+        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
 
 
 def test_decode_zero_length_sequence(hx, oracle):

@@ -39,7 +39,7 @@ def test_noalloc_matches_workspace_entry_point():
     scale = 1.0 / math.sqrt(hd)
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
-    ws = torch.empty(cache.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(cache.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda")
     want = torch.empty((n, Hq * hd), dtype=torch.float16, device="cuda")
     _lib.check(lib.hx_decode_attention(cache.handle, 0, C.c_void_p(q.data_ptr()), _lib.HX_FP16,
                                        C.c_void_p(sid.data_ptr()), C.c_void_p(lens.data_ptr()), n,
