@@ -9,7 +9,9 @@ import ctypes as C
 import os
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libhxkv.so")
+# HXINFER_B200_LIB selects another build of the library (e.g. to compare two
+# builds in one process run); default: the in-tree libhxkv.so.
+LIB_PATH = os.environ.get("HXINFER_B200_LIB") or os.path.join(PKG, "libhxkv.so")
 
 HX_OK, HX_ERR_INVALID, HX_ERR_CAPACITY, HX_ERR_OOM, HX_ERR_CUDA = 0, 1, 2, 3, 4
 HX_ERR_NCCL, HX_ERR_TIMEOUT, HX_ERR_NOT_FOUND, HX_ERR_UNSUPPORTED = 5, 6, 7, 8
