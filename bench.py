@@ -15,7 +15,10 @@ aggregate decode tok/s; the decode kernel's achieved HBM GB/s is in
 Multi-GPU (torchrun, one process per GPU, NCCL): at 8 GPUs each rank holds
 one kv head (4 q heads) of every sequence; at 2 or 4 GPUs each rank holds a
 length-balanced subset of the sequences with all 8 kv heads.  After every
-layer the per-rank attention outputs are all-gathered (NCCL over NVLink).
+layer the per-rank attention outputs are gathered: by default the decode
+kernels store every output row straight into every rank's output buffer over
+NVLink peer memory and post an epoch flag (``--collective p2p``); with
+``--collective nccl`` an NCCL all-gather follows each decode call.
 
 ``--impl reference`` times the reference's CPU attention algorithm (the
 oracle restatement of hxinfer-engine/src/layer/attention.cpp:49-85 with the
@@ -221,8 +224,43 @@ def run_batched_decode(args):
     v_in = torch.randn((LAYERS, n, hkv * HD), generator=g, device=dev).half()
     q_rot = torch.empty_like(q_in)
     out = torch.zeros((LAYERS, n_pad, hq * HD), dtype=torch.float16, device=dev)
+    p2p = world > 1 and args.collective == "p2p"
     gathered = torch.empty((LAYERS, world, n_pad, hq * HD), dtype=torch.float16, device=dev) \
-        if world > 1 else None
+        if world > 1 and not p2p else None
+    peer = None
+    if p2p:
+        # every rank's decode stores its rows straight into every rank's
+        # [LAYERS][NSEQ][HQ*HD] buffer (reference output layout, no assembly)
+        def exchange(blob):
+            allb = [None] * world
+            dist.all_gather_object(allb, blob)
+            return allb
+        peer = kv.PeerGather(rank, world, LAYERS * NSEQ * HQ * HD * 2, exchange)
+        assembled = peer.view(torch.float16, shape=(LAYERS, NSEQ, HQ * HD))
+        out_rows = torch.tensor(seqs, dtype=torch.int32, device=dev)
+        head0 = heads[0] * (HQ // HKV)
+        layer_bytes = NSEQ * HQ * HD * 2
+        epoch = [0]
+
+    def attend(l, lens, timed_events=False):
+        if timed_events:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        if p2p:
+            epoch[0] += 1
+            cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer, out_offset=l * layer_bytes,
+                                out_rows=out_rows, out_row_heads=HQ, out_head0=head0,
+                                epoch=epoch[0], workspace=ws)
+        else:
+            cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
+        if timed_events:
+            e1.record(stream)
+            ev_pairs.append((e0, e1))
+        if p2p:
+            peer.wait(epoch[0])
+        elif world > 1:
+            dist.all_gather_into_tensor(gathered[l], out[l])
     seq_ids = torch.arange(n, dtype=torch.int32, device=dev)
     total_steps = W + 2 * K
     base = torch.from_numpy(my_len.astype(np.int32)).to(dev)
@@ -237,16 +275,7 @@ def run_batched_decode(args):
         for l in range(LAYERS):
             cache.rope_append(l, k_in[l], v_in[l], seq_ids, pos, q=q_in[l], num_q_heads=hq,
                               table=table, q_out=q_rot[l])
-            if timed_events:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
-            if timed_events:
-                e1.record(stream)
-                ev_pairs.append((e0, e1))
-            if world > 1:
-                dist.all_gather_into_tensor(gathered[l], out[l])
+            attend(l, lens, timed_events)
 
     def barrier():
         if world > 1:
@@ -303,7 +332,12 @@ def run_batched_decode(args):
     q_h = q_in.cpu().pin_memory()
     k_h = k_in.cpu().pin_memory()
     v_h = v_in.cpu().pin_memory()
-    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    if p2p:
+        # this rank reads back its share of the assembled output rows
+        r0, r1 = rank * NSEQ // world, (rank + 1) * NSEQ // world
+        out_h = torch.empty((LAYERS, r1 - r0, HQ * HD), dtype=torch.float16).pin_memory()
+    else:
+        out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     q_d, k_d, v_d = torch.empty_like(q_in), torch.empty_like(k_in), torch.empty_like(v_in)
 
     def e2e_step(si):
@@ -314,10 +348,11 @@ def run_batched_decode(args):
         for l in range(LAYERS):
             cache.rope_append(l, k_d[l], v_d[l], seq_ids, pos, q=q_d[l], num_q_heads=hq,
                               table=table, q_out=q_rot[l])
-            cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered[l], out[l])
-        out_h.copy_(out, non_blocking=True)
+            attend(l, lens)
+        if p2p:
+            out_h.copy_(assembled[:, r0:r1], non_blocking=True)
+        else:
+            out_h.copy_(out, non_blocking=True)
 
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -356,6 +391,8 @@ def run_batched_decode(args):
                        "mean_len": float(np.mean(lengths)),
                        "kv_bytes_per_step": float(2 * (lengths.sum() + NSEQ) * HKV * HD * 2 * LAYERS),
                        "parallelism": f"{mode}x{world}",
+                       "collective": ("p2p gather fused into the decode kernels" if p2p else
+                                      "nccl all_gather_into_tensor" if world > 1 else "none"),
                        "l2": "inputs larger than L2 (KV cache >> 126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
@@ -366,10 +403,15 @@ def run_batched_decode(args):
             "cpu_baseline": cpu,
             "e2e": {"value": NSEQ * K / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": K * LAYERS * 3,
+            "gpu_launches": K * LAYERS * (4 if p2p else 3),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank unmaps its buffer while a peer may still write it
+    if peer is not None:
+        peer.close()
     cache.close()
     table.close()
     if world > 1:
@@ -386,6 +428,9 @@ def main():
     ap.add_argument("--workload", default="batched_decode",
                     choices=["batched_decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1: gather fused into the decode kernels over NVLink peer memory "
+                         "(p2p) or an NCCL all-gather after each decode call (nccl)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -70,6 +70,16 @@ SIGNATURES = {
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_kv_restore": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_prefix_hash": (C.c_uint64, [C.POINTER(C.c_int32), C.c_size_t]),
+    "hx_dist_handle_bytes": (C.c_size_t, []),
+    "hx_dist_create": (_I, [_I, _I, C.c_size_t, C.POINTER(_P)]),
+    "hx_dist_export": (_I, [_P, _P]),
+    "hx_dist_connect": (_I, [_P, _P]),
+    "hx_dist_destroy": (_I, [_P]),
+    "hx_dist_buffer": (_P, [_P]),
+    "hx_decode_attention_gather": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P,
+                                        C.c_size_t, _P, _I, _I, _I, _P, C.c_size_t, C.c_uint32,
+                                        _P]),
+    "hx_dist_wait": (_I, [_P, C.c_uint32, _P]),
 }
 
 _lib = None

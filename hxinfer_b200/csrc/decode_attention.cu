@@ -49,8 +49,22 @@ struct DecodeParams {
     const int32_t* lengths;
     int n_seqs, hq, group, q_f32;
     float scale_log2;          // softmax scale * log2(e)
-    void* out;                 // [n_seqs][hq*128]
+    void* out;                 // first destination (== outs[0])
+    // Output placement: q head qh of sequence s goes to row out_rows[s]
+    // (s when out_rows is null), column block out_head0 + qh, of a matrix
+    // [rows][out_hq * head_dim] in every destination outs[0..n_outs).  A plain
+    // call has one destination, out_hq == hq and out_head0 == 0; a gathering
+    // call also writes each other rank's buffer.
+    void* outs[kHxMaxRanks];
+    int n_outs;
+    const int32_t* out_rows;
+    int out_hq, out_head0;
+    int out_row_limit;         // rows the destinations hold; a row beyond is skipped and recorded
+    int out_vec;               // every destination is 16-byte aligned: rows go out as 16-byte stores
     int out_f32;
+    unsigned int* peer_flags[kHxMaxRanks];   // epoch words to post on the other ranks
+    int n_flags;
+    unsigned int epoch;
     float* ws_o;               // [slots][group][128]
     float2* ws_ml;             // [slots][group] (m, l)
     int* status;
@@ -189,13 +203,74 @@ __device__ __forceinline__ int cta_of_tile(const int* cstart, int n_eff, int g)
     return lo;
 }
 
-__device__ __forceinline__ void store_out(const DecodeParams& p, int s, int h, int r, int d, float val)
+// Index, in q-head units, of the first q head of sequence s in the output,
+// or -1 (recorded) when its row lies outside the destinations.
+__device__ __forceinline__ int64_t out_head_base(const DecodeParams& p, int s)
 {
-    const int64_t oi = ((int64_t)s * p.hq + (int64_t)h * p.group + r) * 128 + d;
-    if (p.out_f32)
-        static_cast<float*>(p.out)[oi] = val;
-    else
-        static_cast<__half*>(p.out)[oi] = __float2half_rn(val);
+    const int row = p.out_rows ? p.out_rows[s] : s;
+    if (row < 0 || row >= p.out_row_limit) {
+        record_status(p.status, HX_ERR_CAPACITY);
+        return -1;
+    }
+    return (int64_t)row * p.out_hq + p.out_head0;
+}
+
+// Gathering calls post the call's epoch on every other rank once every row
+// this rank stored is performed system-wide.  post_epoch_kernel does it:
+// launched after the decode kernels as an ordinary stream launch, it starts
+// only when all of them have completed (their stores performed), then
+// fences at system scope and stores the epoch into each peer's flag word
+// with release semantics, so a rank that acquires the epoch also sees every
+// row this rank stored into its buffer.
+__global__ void post_epoch_kernel(const DecodeParams p)
+{
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    for (int k = 0; k < p.n_flags; ++k)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[k]), "r"(p.epoch)
+                     : "memory");
+}
+
+// Stores n_rows finished rows (fp32 in shared memory, 128 dims each, row r
+// at src + r * src_stride) as q heads qh0 .. qh0 + n_rows - 1 of sequence s
+// into every destination, threads tid, tid + nthr, ... each taking one
+// 16-byte chunk of one row of one destination at a time (so a row crosses
+// NVLink as full 16-byte writes).  Rounds like store_out.
+__device__ void store_rows(const DecodeParams& p, int s, int qh0, const float* src, int src_stride,
+                           int n_rows, int tid, int nthr)
+{
+    const int64_t base = out_head_base(p, s);
+    if (base < 0) return;
+    if (!p.out_vec) {
+        for (int idx = tid; idx < n_rows * 128; idx += nthr) {
+            const int r = idx / 128, d = idx % 128;
+            const float val = src[r * src_stride + d];
+            const int64_t oi = (base + qh0 + r) * 128 + d;
+            for (int k = 0; k < p.n_outs; ++k) {
+                if (p.out_f32) static_cast<float*>(p.outs[k])[oi] = val;
+                else static_cast<__half*>(p.outs[k])[oi] = __float2half_rn(val);
+            }
+        }
+        return;
+    }
+    const int chunks = p.out_f32 ? 32 : 16;  // 16-byte chunks per row
+    const int per_dest = n_rows * chunks;
+    for (int idx = tid; idx < p.n_outs * per_dest; idx += nthr) {
+        const int k = idx / per_dest, rem = idx - k * per_dest;
+        const int r = rem / chunks, c = rem - r * chunks;
+        const float* f = src + r * src_stride;
+        const int64_t row = (base + qh0 + r) * 128;
+        if (p.out_f32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(p.outs[k]) + row + 4 * c) =
+                *reinterpret_cast<const float4*>(f + 4 * c);
+        } else {
+            const float4 a = *reinterpret_cast<const float4*>(f + 8 * c);
+            const float4 b = *reinterpret_cast<const float4*>(f + 8 * c + 4);
+            *reinterpret_cast<uint4*>(static_cast<__half*>(p.outs[k]) + row + 8 * c) =
+                make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                           pack_half2(b.z, b.w));
+        }
+    }
 }
 
 // Sequences with no positions attend to nothing: their rows are zeros.
@@ -207,10 +282,14 @@ __device__ void zero_empty_outputs(const DecodeParams& p)
         if (len >= 1 && len <= p.view.capacity) continue;
         if (lane == 0) record_status(p.status, HX_ERR_CAPACITY);
         if (len >= 1) continue;  // over capacity: clamped, still attended
+        const int64_t base = out_head_base(p, s);
+        if (base < 0) continue;
         for (int e = lane; e < p.hq * 128; e += 32) {
-            const int64_t oi = (int64_t)s * p.hq * 128 + e;
-            if (p.out_f32) static_cast<float*>(p.out)[oi] = 0.f;
-            else static_cast<__half*>(p.out)[oi] = __float2half_rn(0.f);
+            const int64_t oi = base * 128 + e;
+            for (int k = 0; k < p.n_outs; ++k) {
+                if (p.out_f32) static_cast<float*>(p.outs[k])[oi] = 0.f;
+                else static_cast<__half*>(p.outs[k])[oi] = __float2half_rn(0.f);
+            }
         }
     }
 }
@@ -309,6 +388,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     float o[16][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     bool piece_from_seg_start = false;
+    bool dead = false;  // a bounded wait ran out
     const uint32_t stage_base = smem_u32(&sm.stage[0][0][0]);
     // ldmatrix row addresses (before swizzle) for this lane
     const int lm_mi = lane >> 3, lm_r = lane & 7;
@@ -348,9 +428,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
 
         const int st = i % kDecStages;
-        if (!mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1)) {
-            record_status(p.status, HX_ERR_TIMEOUT);
-            return;
+        if (!dead) {
+            const bool ok = mbar_wait(&sm.full[st], (uint32_t)(i / kDecStages) & 1);
+            if (__any_sync(0xffffffffu, !ok)) {
+                // The tile never arrived: record it and stop waiting, but keep
+                // running the loop (on stale shared memory, in bounds) so the
+                // other consumer warps never wait on this one at a named
+                // barrier.  The output of this call is then invalid.
+                if (lane == 0) record_status(p.status, HX_ERR_TIMEOUT);
+                dead = true;
+            }
         }
         const int valid = min(kBlockTokens, cur.len - cur.j * kBlockTokens);
         const uint32_t kb = stage_base + st * 2 * kTileBytes;
@@ -517,11 +604,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     acc += wgt * sm.merge_o[ww][r][d];
                 }
                 if (whole) {
-                    store_out(p, cur.s, cur.h, r, d, acc / L);
+                    // each thread reads only its own dim d of merge_o: the
+                    // finished row can replace warp 0's partial in place
+                    sm.merge_o[0][r][d] = acc / L;
                 } else {
                     p.ws_o[((int64_t)slot * p.group + r) * 128 + d] = acc;
                     if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
                 }
+            }
+            if (whole) {
+                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                store_rows(p, cur.s, cur.h * p.group, &sm.merge_o[0][0][0], 128, p.group, d,
+                           kDecConsumerWarps * 32);
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
         }
@@ -538,18 +632,25 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 // range starts inside the segment, merged in that fixed order: warp 0 loads
 // every piece's (m, l) in one round and leaves normalised weights in shared
 // memory; each thread then loads its dim of every piece in one round.
+//
+// Items (segment, q row) are numbered seg * group + r; CTA b takes items b,
+// b + gridDim.x, ...; the launch gives one CTA per item, since each item is
+// a short chain of dependent loads and they overlap best as separate CTAs.
 __global__ void __launch_bounds__(128)
     decode_combine_kernel(const DecodeParams p, int grid_ctas)
 {
     pdl_trigger();
-    const int seg = blockIdx.x, r = blockIdx.y;
     const int hkv = p.view.hkv;
-    const int s = seg / hkv, h = seg % hkv;
+    const int n_items = p.n_seqs * hkv * p.group;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     __shared__ int sh_range[4];  // a, b, T, n_eff
     __shared__ int slot_list[kMaxPieces];
     __shared__ float weights[kMaxPieces];
+    __shared__ __align__(16) float row_buf[128];
     __shared__ int sh_np;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int seg = item / p.group, r = item % p.group;
+    const int s = seg / hkv, h = seg % hkv;
     if (warp == 0) {
         int before = 0, total = 0;
         for (int base = 0; base < p.n_seqs; base += 32) {
@@ -577,9 +678,9 @@ __global__ void __launch_bounds__(128)
     }
     __syncthreads();
     const int a = sh_range[0], b = sh_range[1], T = sh_range[2], n_eff = sh_range[3];
-    if (a >= b || T == 0) return;
     auto cstart = [&](int c) { return (int)((long long)T * c / n_eff); };
-    if (t == 0) {
+    if (t == 0) sh_np = 0;
+    if (t == 0 && a < b && T > 0) {
         int c = (int)((long long)a * n_eff / T);
         while (c + 1 < n_eff && cstart(c + 1) <= a) ++c;
         while (c > 0 && cstart(c) > a) --c;
@@ -591,10 +692,9 @@ __global__ void __launch_bounds__(128)
         sh_np = np;
     }
     __syncthreads();
-    const int np = sh_np;
-    if (np <= 1) return;  // one piece: the decode kernel wrote the output
-    pdl_wait();           // the pieces come from the decode grid
-    if (warp == 0) {
+    const int np = sh_np;  // <= 1: the decode kernel wrote this output itself
+    if (np > 1) pdl_wait();  // the pieces come from the decode grid
+    if (np > 1 && warp == 0) {
         constexpr int kPerLane = (kMaxPieces + 31) / 32;
         float2 ml[kPerLane];
 #pragma unroll
@@ -639,7 +739,13 @@ __global__ void __launch_bounds__(128)
         for (int u = 0; u < kBatch; ++u)
             if (q0 + u < np) acc += weights[q0 + u] * v[u];
     }
-    store_out(p, s, h, r, t, acc);
+    if (np > 1) {
+        row_buf[t] = acc;
+        __syncthreads();
+        store_rows(p, s, h * p.group + r, row_buf, 128, 1, t, 128);
+    }
+    __syncthreads();  // shared state is rewritten by the next item
+    }
 }
 
 // Any head_dim (<= 256), any group: one CTA of 4 warps per (sequence, q
@@ -715,8 +821,13 @@ __global__ void __launch_bounds__(128)
             o += wgt * sm_o[ww][d];
         }
         const float val = L > 0.f ? o / L : 0.f;
-        if (p.out_f32) static_cast<float*>(p.out)[qoff + d] = val;
-        else static_cast<__half*>(p.out)[qoff + d] = __float2half_rn(val);
+        const int64_t base = out_head_base(p, s);
+        if (base < 0) break;
+        const int64_t ooff = (base + qh) * hd;
+        for (int k = 0; k < p.n_outs; ++k) {
+            if (p.out_f32) static_cast<float*>(p.outs[k])[ooff + d] = val;
+            else static_cast<__half*>(p.outs[k])[ooff + d] = __float2half_rn(val);
+        }
     }
 }
 
@@ -756,8 +867,8 @@ static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas
                                   smem, stream, ov, c->tm_k, c->tm_v, p);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention_kernel launch");
     if (int rc = check_launch("decode_attention_kernel")) return rc;
-    e = launch_kernel(decode_combine_kernel, dim3(p.n_seqs * p.view.hkv, p.group), dim3(128), 0,
-                      stream, true, p, n_ctas);
+    const int n_items = p.n_seqs * p.view.hkv * p.group;
+    e = launch_kernel(decode_combine_kernel, dim3(n_items), dim3(128), 0, stream, true, p, n_ctas);
     if (e != cudaSuccess) return cuda_fail(e, "decode_combine_kernel launch");
     return check_launch("decode_combine_kernel");
 }
@@ -774,23 +885,30 @@ extern "C" size_t hx_decode_workspace_bytes(const hx_kv_cache* c, int n_seqs, in
     return decode_ws_bytes(n_seqs, hkv, group < 1 ? 1 : group, std::min(num_sms(), kMaxPieces - 2));
 }
 
-extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
-                                   const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
-                                   int num_q_heads, float scale, void* out, int out_dtype,
-                                   void* workspace, size_t workspace_bytes, hx_stream_t stream)
+namespace hx {
+
+static int validate_decode(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
+                           const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                           int num_q_heads, int out_dtype)
 {
     if (!c) return fail(HX_ERR_INVALID, "null cache");
     if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
-    if (!q || !seq_ids || !lengths || !out) return fail(HX_ERR_INVALID, "null q/seq_ids/lengths/out");
-    if (n_seqs < 0) return fail(HX_ERR_INVALID, "n_seqs < 0");
-    if (n_seqs > c->cfg.max_seqs) return fail(HX_ERR_INVALID, "n_seqs %d > max_seqs %d", n_seqs, c->cfg.max_seqs);
-    const int hkv = c->cfg.num_kv_heads, hd = c->cfg.head_dim;
+    if (n_seqs < 0 || n_seqs > c->cfg.max_seqs)
+        return fail(HX_ERR_INVALID, "n_seqs %d outside [0, %d]", n_seqs, c->cfg.max_seqs);
+    if (n_seqs > 0 && (!q || !seq_ids || !lengths)) return fail(HX_ERR_INVALID, "null q/seq_ids/lengths");
+    const int hkv = c->cfg.num_kv_heads;
     if (num_q_heads < hkv || num_q_heads % hkv)
         return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
     if ((q_dtype != HX_FP16 && q_dtype != HX_FP32) || (out_dtype != HX_FP16 && out_dtype != HX_FP32))
         return fail(HX_ERR_INVALID, "q/out dtype");
-    if (n_seqs == 0) return HX_OK;
-    const int group = num_q_heads / hkv;
+    return HX_OK;
+}
+
+// Everything but the output placement (set by the caller afterwards).
+static DecodeParams base_params(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
+                                const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                                int num_q_heads, float scale, int out_dtype)
+{
     DecodeParams p{};
     p.view = make_view(c, layer);
     p.q = q;
@@ -799,25 +917,126 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
     p.lengths = lengths;
     p.n_seqs = n_seqs;
     p.hq = num_q_heads;
-    p.group = group;
+    p.group = num_q_heads / c->cfg.num_kv_heads;
     p.scale_log2 = scale * 1.4426950408889634f;
-    p.out = out;
+    p.out_hq = num_q_heads;
+    p.out_row_limit = n_seqs;
     p.out_f32 = out_dtype == HX_FP32;
-    p.status = status_word();
-    cudaStream_t s = (cudaStream_t)stream;
-    const bool fast = c->has_tmap && hd == 128 && group <= 16;
-    if (!fast) {
-        decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
+    return p;
+}
+
+static bool fast_path(const hx_kv_cache* c, const DecodeParams& p)
+{
+    return c->has_tmap && c->cfg.head_dim == 128 && p.group <= 16;
+}
+
+// Launches the decode of a filled-in parameter block (n_seqs >= 1).  The
+// fast path needs `scratch` of decode_ws_bytes, checked by the caller.
+static int run_decode(const hx_kv_cache* c, DecodeParams& p, void* scratch, cudaStream_t s)
+{
+    if (!fast_path(c, p)) {
+        decode_generic_kernel<<<p.n_seqs * p.hq, 128, 0, s>>>(p);
         return check_launch("decode_generic_kernel");
     }
     const int n_ctas = std::min(num_sms(), kMaxPieces - 2);
-    const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
-    if (!workspace || workspace_bytes < need)
+    bind_workspace(p, scratch, n_ctas);
+    if (p.group <= 8) return launch_decode<8>(c, p, n_ctas, s);
+    return launch_decode<16>(c, p, n_ctas, s);
+}
+
+static size_t needed_scratch(const hx_kv_cache* c, const DecodeParams& p)
+{
+    if (!fast_path(c, p)) return 0;
+    return decode_ws_bytes(p.n_seqs, p.view.hkv, p.group, std::min(num_sms(), kMaxPieces - 2));
+}
+
+}  // namespace hx
+
+extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
+                                   const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                                   int num_q_heads, float scale, void* out, int out_dtype,
+                                   void* workspace, size_t workspace_bytes, hx_stream_t stream)
+{
+    if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 out_dtype))
+        return rc;
+    if (n_seqs > 0 && !out) return fail(HX_ERR_INVALID, "null out");
+    if (n_seqs == 0) return HX_OK;
+    DecodeParams p = base_params(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 scale, out_dtype);
+    p.out = out;
+    p.outs[0] = out;
+    p.n_outs = 1;
+    p.out_vec = reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    p.status = status_word();
+    const size_t need = needed_scratch(c, p);
+    if (need && (!workspace || workspace_bytes < need))
         return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
                     workspace_bytes, need);
-    bind_workspace(p, workspace, n_ctas);
-    if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
-    return launch_decode<16>(c, p, n_ctas, s);
+    return run_decode(c, p, workspace, (cudaStream_t)stream);
+}
+
+// Gathering decode: the rows go to every rank's buffer and the last CTA
+// posts the epoch (hx_dist state lives in dist.cu).
+extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const void* q,
+                                          int q_dtype, const int32_t* seq_ids,
+                                          const int32_t* lengths, int n_seqs, int num_q_heads,
+                                          float scale, hx_dist* dist, size_t out_offset,
+                                          const int32_t* out_rows, int out_row_heads,
+                                          int out_head0, int out_dtype, void* workspace,
+                                          size_t workspace_bytes, uint32_t epoch,
+                                          hx_stream_t stream)
+{
+    if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 out_dtype))
+        return rc;
+    if (!dist || !dist->connected) return fail(HX_ERR_INVALID, "gather endpoint is not connected");
+    int dev = -1;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != dist->device || dev != c->device)
+        return fail(HX_ERR_INVALID, "current device %d, endpoint on %d, cache on %d", dev,
+                    dist->device, c->device);
+    if (n_seqs > 0 && !out_rows) return fail(HX_ERR_INVALID, "null out_rows");
+    if (out_head0 < 0 || out_row_heads < num_q_heads || out_head0 + num_q_heads > out_row_heads)
+        return fail(HX_ERR_INVALID, "q heads [%d, %d) do not fit an output row of %d heads",
+                    out_head0, out_head0 + num_q_heads, out_row_heads);
+    if (out_offset % 16) return fail(HX_ERR_INVALID, "out_offset %zu is not 16-byte aligned", out_offset);
+    const size_t esize = out_dtype == HX_FP32 ? 4 : 2;
+    const size_t row_bytes = (size_t)out_row_heads * c->cfg.head_dim * esize;
+    if (out_offset > dist->bytes || (dist->bytes - out_offset) / row_bytes < 1)
+        return fail(HX_ERR_CAPACITY, "gather buffer of %zu bytes holds no row at offset %zu",
+                    dist->bytes, out_offset);
+    const size_t rows = (dist->bytes - out_offset) / row_bytes;
+    DecodeParams p = base_params(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 scale, out_dtype);
+    p.n_outs = 0;
+    for (int r = 0; r < dist->world; ++r) {
+        // own buffer first: it is the destination the single-destination paths use
+        const int rr = (dist->rank + r) % dist->world;
+        p.outs[p.n_outs++] = dist->peer_buf[rr] + out_offset;
+    }
+    p.out = p.outs[0];
+    p.out_vec = 1;  // buffers from cudaMalloc, offset a multiple of 16
+    p.out_rows = out_rows;
+    p.out_hq = out_row_heads;
+    p.out_head0 = out_head0;
+    p.out_row_limit = rows > (size_t)INT32_MAX ? INT32_MAX : (int)rows;
+    p.n_flags = 0;
+    for (int r = 0; r < dist->world; ++r)
+        if (r != dist->rank) p.peer_flags[p.n_flags++] = dist->peer_flags[r] + dist->rank;
+    p.epoch = epoch;
+    p.status = status_word();
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n_seqs > 0) {
+        const size_t need = needed_scratch(c, p);
+        if (need && (!workspace || workspace_bytes < need))
+            return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
+                        workspace_bytes, need);
+        if (int rc = run_decode(c, p, workspace, s)) return rc;
+    }
+    if (p.n_flags == 0) return HX_OK;
+    post_epoch_kernel<<<1, 32, 0, s>>>(p);
+    return check_launch("post_epoch_kernel");
 }
 
 // ---------------------------------------------------------------- no-allocation variant
@@ -869,46 +1088,28 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
                                            float scale, void* out, int out_dtype,
                                            hx_stream_t stream)
 {
-    if (!c) return fail(HX_ERR_INVALID, "null cache");
-    if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
-    if (!q || !seq_ids || !lengths || !out) return fail(HX_ERR_INVALID, "null q/seq_ids/lengths/out");
-    if (n_seqs < 0 || n_seqs > c->cfg.max_seqs)
-        return fail(HX_ERR_INVALID, "n_seqs %d outside [0, %d]", n_seqs, c->cfg.max_seqs);
-    const int hkv = c->cfg.num_kv_heads, hd = c->cfg.head_dim;
-    if (num_q_heads < hkv || num_q_heads % hkv)
-        return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
-    if ((q_dtype != HX_FP16 && q_dtype != HX_FP32) || (out_dtype != HX_FP16 && out_dtype != HX_FP32))
-        return fail(HX_ERR_INVALID, "q/out dtype");
+    if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 out_dtype))
+        return rc;
+    if (n_seqs > 0 && !out) return fail(HX_ERR_INVALID, "null out");
     if (n_seqs == 0) return HX_OK;
-    const int group = num_q_heads / hkv;
-    const int n_ctas = std::min(num_sms(), kMaxPieces - 2);
-    const size_t need = decode_ws_bytes(n_seqs, hkv, group, n_ctas);
+    DecodeParams p = base_params(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 scale, out_dtype);
+    p.out = out;
+    p.outs[0] = out;
+    p.n_outs = 1;
+    p.out_vec = reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    p.status = nullptr;
+    const size_t need = needed_scratch(c, p);
     if (need > kNoAllocScratchBytes)
         return fail(HX_ERR_CAPACITY,
                     "this call needs %zu bytes of split-K scratch; the no-allocation entry point "
                     "holds at most %zu (use hx_decode_attention with a caller workspace)",
                     need, kNoAllocScratchBytes);
-    void* scratch = noalloc_scratch_ptr();
-    if (!scratch) return fail(HX_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch failed");
-    DecodeParams p{};
-    p.view = make_view(c, layer);
-    p.q = q;
-    p.q_f32 = q_dtype == HX_FP32;
-    p.seq_ids = seq_ids;
-    p.lengths = lengths;
-    p.n_seqs = n_seqs;
-    p.hq = num_q_heads;
-    p.group = group;
-    p.scale_log2 = scale * 1.4426950408889634f;
-    p.out = out;
-    p.out_f32 = out_dtype == HX_FP32;
-    p.status = nullptr;
-    cudaStream_t s = (cudaStream_t)stream;
-    if (!(c->has_tmap && hd == 128 && group <= 16)) {
-        decode_generic_kernel<<<n_seqs * num_q_heads, 128, 0, s>>>(p);
-        return check_launch("decode_generic_kernel");
+    void* scratch = nullptr;
+    if (need) {
+        scratch = noalloc_scratch_ptr();
+        if (!scratch) return fail(HX_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch failed");
     }
-    bind_workspace(p, scratch, n_ctas);
-    if (group <= 8) return launch_decode<8>(c, p, n_ctas, s);
-    return launch_decode<16>(c, p, n_ctas, s);
+    return run_decode(c, p, scratch, (cudaStream_t)stream);
 }

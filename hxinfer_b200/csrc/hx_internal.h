@@ -53,6 +53,21 @@ struct hx_kv_cache {
     char* tm_v_base = nullptr;
 };
 
+// Peer-to-peer gather of decode outputs across the GPUs of one node: every
+// rank owns a gather buffer and a flag word per rank, exported by CUDA IPC
+// and mapped into every other rank.
+constexpr int kHxMaxRanks = 8;
+
+struct hx_dist {
+    int rank = 0, world = 1, device = 0;
+    size_t bytes = 0;
+    char* buf = nullptr;                 // local gather buffer
+    unsigned int* flags = nullptr;       // local [world] epochs posted by each rank
+    char* peer_buf[kHxMaxRanks] = {};    // every rank's buffer (own at [rank])
+    unsigned int* peer_flags[kHxMaxRanks] = {};
+    bool connected = false;
+};
+
 struct hx_rope_table {
     hx_rope_config cfg{};
     float2* d_cos_sin = nullptr;  // [max_pos][head_dim/2] (cos, sin)

@@ -59,7 +59,10 @@ def assemble(mode: str, parts, shards, n_seqs: int, n_q_heads: int, head_dim: in
     n_kv = max(h for _, hs in shards for h in hs) + 1
     group = n_q_heads // n_kv
     for part, (seqs, heads) in zip(parts, shards):
+        if not len(seqs):
+            continue  # a rank without sequences contributes nothing
         part = np.asarray(part).reshape(len(seqs), len(heads), group * head_dim)
+        rows = np.asarray(seqs, dtype=np.int64)
         for j, h in enumerate(heads):
-            out[np.array(seqs), h * group * head_dim:(h + 1) * group * head_dim] = part[:, j]
+            out[rows, h * group * head_dim:(h + 1) * group * head_dim] = part[:, j]
     return out

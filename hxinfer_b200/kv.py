@@ -197,6 +197,31 @@ class KVCache:
                                          _stream(stream)), "decode attention")
         return out
 
+    def decode_gather(self, layer: int, q: torch.Tensor, seq_ids: torch.Tensor,
+                      lengths: torch.Tensor, num_q_heads: int, gather: "PeerGather", *,
+                      out_offset: int, out_rows: torch.Tensor, out_row_heads: int,
+                      out_head0: int, epoch: int, scale: float | None = None,
+                      out_dtype=torch.float16, workspace: torch.Tensor | None = None,
+                      stream=None):
+        """Decode attention of this rank's shard with the outputs stored into
+        every rank's gather buffer (hx_decode_attention_gather): q head qh of
+        local sequence s lands in row out_rows[s], column block out_head0+qh,
+        of the [rows][out_row_heads*head_dim] matrix at byte out_offset.
+        Follow it by ``gather.wait(epoch)`` before reading the buffer."""
+        _need_cuda(q, seq_ids, lengths, out_rows, workspace)
+        n = seq_ids.numel()
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if workspace is None:
+            workspace = torch.zeros(max(self.workspace_bytes(n, num_q_heads), 16),
+                                    dtype=torch.uint8, device=q.device)
+        odt = HX_FP32 if out_dtype == torch.float32 else HX_FP16
+        check(load().hx_decode_attention_gather(
+            self.handle, layer, _ptr(q), _dt(q), _ptr(seq_ids), _ptr(lengths), n, num_q_heads,
+            scale, gather.handle, out_offset, _ptr(out_rows), out_row_heads, out_head0, odt,
+            _ptr(workspace), workspace.numel() * workspace.element_size(), epoch & 0xFFFFFFFF,
+            _stream(stream)), "decode attention (gather)")
+
     def prefill(self, layer: int, q: torch.Tensor, seq: int, start: int, num_q_heads: int, *,
                 scale: float | None = None, out: torch.Tensor | None = None,
                 out_dtype=torch.float16, stream=None):
@@ -229,3 +254,60 @@ class KVCache:
         _need_cuda(src)
         check(load().hx_kv_restore(self.handle, seq, prefix_len, _ptr(src),
                                    src.numel() * src.element_size(), _stream(stream)), "restore")
+
+
+class PeerGather:
+    """This rank's gather endpoint (hx_dist_*): a device buffer that every
+    rank's decode kernels write into over NVLink peer memory, plus the epoch
+    flags the kernels post.  Construct on every rank with the current device
+    set; ``exchange`` is a callable that all-gathers one bytes object per
+    rank (e.g. built on torch.distributed.all_gather_object) and returns the
+    list in rank order."""
+
+    def __init__(self, rank: int, world: int, buffer_bytes: int, exchange):
+        lib = load()
+        h = C.c_void_p()
+        check(lib.hx_dist_create(rank, world, buffer_bytes, C.byref(h)), "dist create")
+        self.handle = h
+        self.rank, self.world, self.bytes = rank, world, buffer_bytes
+        n = int(lib.hx_dist_handle_bytes())
+        mine = (C.c_char * n)()
+        check(lib.hx_dist_export(self.handle, mine), "dist export")
+        blobs = exchange(bytes(mine))
+        if len(blobs) != world or any(len(b) != n for b in blobs):
+            raise ValueError("exchange must return one handle per rank")
+        allh = (C.c_char * (n * world)).from_buffer_copy(b"".join(blobs))
+        check(lib.hx_dist_connect(self.handle, allh), "dist connect")
+        self.ptr = int(lib.hx_dist_buffer(self.handle))
+
+    def view(self, dtype=torch.float16, offset: int = 0, shape=None) -> torch.Tensor:
+        """A tensor over this rank's buffer (no copy; valid while the endpoint lives)."""
+        esize = torch.empty((), dtype=dtype).element_size()
+        numel = (self.bytes - offset) // esize
+        if shape is not None:
+            numel = math.prod(shape)
+        storage = torch.cuda.current_device()
+        return _tensor_at(self.ptr + offset, numel, dtype, storage, self).view(
+            *(shape if shape is not None else (numel,)))
+
+    def wait(self, epoch: int, stream=None):
+        check(load().hx_dist_wait(self.handle, epoch & 0xFFFFFFFF, _stream(stream)), "dist wait")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            check(load().hx_dist_destroy(self.handle), "dist destroy")
+            self.handle = None
+
+
+def _tensor_at(ptr: int, numel: int, dtype, device: int, owner) -> torch.Tensor:
+    """Non-owning tensor over device memory at ptr (keeps `owner` referenced)."""
+    class _Holder:
+        pass
+    holder = _Holder()
+    holder.__cuda_array_interface__ = {
+        "shape": (numel,), "typestr": {torch.float16: "<f2", torch.float32: "<f4",
+                                        torch.uint8: "|u1", torch.int32: "<i4"}[dtype],
+        "data": (ptr, False), "version": 3, "strides": None}
+    holder.owner = owner
+    with torch.cuda.device(device):
+        return torch.as_tensor(holder, device=torch.device("cuda", device))

@@ -228,6 +228,68 @@ int hx_decode_attention_noalloc(const hx_kv_cache* cache, int layer, const void*
                                 int num_q_heads, float scale, void* out, int out_dtype,
                                 hx_stream_t stream);
 
+/* ------------------------------------------------------------ multi-GPU gather
+ *
+ * K5: decode attention sharded over the GPUs of one node (one process per
+ * GPU), with the all-gather of the per-rank outputs fused into the decode
+ * kernels.  Each rank owns a gather buffer; the decode and combine kernels
+ * store every output row of this rank into every rank's buffer over NVLink
+ * peer memory (16-byte stores, no bulk copy), and a one-thread kernel
+ * launched after them posts the call's epoch into a flag word on every other
+ * rank.  hx_dist_wait then holds the stream until every other rank's epoch
+ * has arrived.  The
+ * reference engine is single-GPU; this replaces an NCCL all-gather issued
+ * after each decode call.
+ *
+ * Set-up, on every rank (with the current device set to the rank's GPU):
+ *   hx_dist_create -> hx_dist_export -> exchange the handles (any host-side
+ *   all-gather, e.g. torch.distributed over a store) -> hx_dist_connect.
+ * All ranks must run on GPUs of one node that can access each other's memory
+ * (cudaDeviceCanAccessPeer), in different processes. */
+typedef struct hx_dist hx_dist;
+
+/* Bytes of the IPC handle blob hx_dist_export writes. */
+size_t hx_dist_handle_bytes(void);
+/* Allocates this rank's gather buffer (buffer_bytes, zeroed) and flag words on
+ * the current device.  1 <= world <= 8, 0 <= rank < world. */
+int hx_dist_create(int rank, int world, size_t buffer_bytes, hx_dist** out);
+/* Writes this rank's IPC handles (hx_dist_handle_bytes bytes) to `handle`. */
+int hx_dist_export(const hx_dist* dist, void* handle);
+/* Maps every other rank's buffer and flags.  handles: world blobs of
+ * hx_dist_handle_bytes each, in rank order (this rank's own is ignored). */
+int hx_dist_connect(hx_dist* dist, const void* handles);
+/* Unmaps the peers and frees this rank's buffer.  Every rank must have
+ * finished its last gathering call (e.g. a host barrier after a device
+ * synchronise) before any rank destroys its endpoint. */
+int hx_dist_destroy(hx_dist* dist);
+/* Device address of this rank's gather buffer. */
+void* hx_dist_buffer(const hx_dist* dist);
+
+/* hx_decode_attention for this rank's shard, with the outputs written into
+ * every rank's gather buffer.  The output is a matrix starting at byte
+ * out_offset of each buffer, [rows][out_row_heads*128] in out_dtype: q head
+ * qh of local sequence s goes to row out_rows[s] (device int32 [n_seqs]),
+ * column block out_head0 + qh.  The ranks' (row, column) blocks must not
+ * overlap.  epoch: a value greater (mod 2^32) than that of this endpoint's
+ * previous call, the same on every rank for the same step.  Every rank makes
+ * the same sequence of calls (also with n_seqs == 0, which only signals).
+ *
+ * The call does not wait for the other ranks: follow it by hx_dist_wait
+ * before reading the buffer.  A region of the buffer may be written again
+ * once every rank has consumed it; with two regions used alternately that
+ * holds when each rank consumes a region before its next gathering call. */
+int hx_decode_attention_gather(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
+                               const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
+                               int num_q_heads, float scale, hx_dist* dist, size_t out_offset,
+                               const int32_t* out_rows, int out_row_heads, int out_head0,
+                               int out_dtype, void* workspace, size_t workspace_bytes,
+                               uint32_t epoch, hx_stream_t stream);
+/* Holds `stream` until every other rank has posted `epoch` (a one-CTA kernel
+ * polling this rank's flag words).  The wait is bounded (4 s); when it runs
+ * out the kernel records HX_ERR_TIMEOUT in the device status word and
+ * returns, so the host finds the failure through hx_device_status. */
+int hx_dist_wait(hx_dist* dist, uint32_t epoch, hx_stream_t stream);
+
 /* ------------------------------------------------------------ prefix snapshots */
 
 /* Bytes of a snapshot of the first prefix_len positions of one sequence:

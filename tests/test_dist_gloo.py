@@ -96,3 +96,13 @@ def test_plan_shapes():
     mode, shards = D.plan(8, 8, lengths)
     assert mode == "kv_heads" and [h for _, h in shards] == [[r] for r in range(8)]
     assert all(len(s) == 64 for s, _ in shards)
+
+
+def test_assemble_with_a_rank_without_sequences():
+    """Fewer sequences than ranks: the empty shard contributes no rows."""
+    mode, shards = D.plan(2, 4, [300])
+    assert mode == "sequences" and shards[1][0] == []
+    part0 = np.arange(8 * 4, dtype=np.float32).reshape(1, 32)
+    part1 = np.zeros((0, 32), np.float32)
+    out = D.assemble(mode, [part0, part1], shards, 1, 8, 4)
+    assert np.array_equal(out, part0)

@@ -234,6 +234,30 @@ def test_decode_repeated_calls_share_workspace(hx, oracle):
     assert_close(outs[0][0].float().cpu().numpy(), want, "32k after repeats")
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_decode_unaligned_out_matches_aligned(hx, out_dtype):
+    """An output pointer that is not 16-byte aligned takes the element-wise
+    store path; its rows equal the aligned call's bit for bit."""
+    rng = np.random.default_rng(65)
+    Hq, Hkv, lengths = 32, 8, [3000, 64, 700]
+    cache = make_cache(hx, 1, Hkv, 3, 3000)
+    for s, L in enumerate(lengths):
+        cache.reserve(s, L)
+    cache.fill_normal(66)
+    q = torch.from_numpy(rng.standard_normal((3, Hq * 128)).astype(np.float16)).cuda()
+    sid = torch.arange(3, dtype=torch.int32, device="cuda")
+    lens = dev(np.array(lengths, np.int32))
+    aligned = cache.decode(0, q, sid, lens, Hq, out_dtype=out_dtype)
+    buf = torch.zeros(3 * Hq * 128 + 1, dtype=out_dtype, device="cuda")
+    shifted = buf[1:].view(3, Hq * 128)
+    assert shifted.data_ptr() % 16 != 0
+    cache.decode(0, q, sid, lens, Hq, out=shifted)
+    torch.cuda.synchronize()
+    hx.device_status()
+    assert torch.equal(shifted.cpu(), aligned.cpu())
+    assert buf[0].item() == 0
+
+
 def test_decode_cuda_graph_replays(hx, oracle):
     """A captured append+decode step replays correctly many times on one
     workspace (the per-segment tickets reset themselves)."""
