@@ -17,8 +17,9 @@ one kv head (4 q heads) of every sequence; at 2 or 4 GPUs each rank holds a
 length-balanced subset of the sequences with all 8 kv heads.  After every
 layer the per-rank attention outputs are gathered: by default the decode
 kernels store every output row straight into every rank's output buffer over
-NVLink peer memory and post an epoch flag (``--collective p2p``); with
-``--collective nccl`` an NCCL all-gather follows each decode call.
+NVLink peer memory, then the ranks exchange an epoch flag
+(``--collective p2p``); with ``--collective nccl`` an NCCL all-gather follows
+each decode call.
 
 ``--impl reference`` times the reference's CPU attention algorithm (the
 oracle restatement of hxinfer-engine/src/layer/attention.cpp:49-85 with the
@@ -251,7 +252,7 @@ def run_batched_decode(args):
             epoch[0] += 1
             cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer, out_offset=l * layer_bytes,
                                 out_rows=out_rows, out_row_heads=HQ, out_head0=head0,
-                                epoch=epoch[0], workspace=ws)
+                                workspace=ws)
         else:
             cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
         if timed_events:

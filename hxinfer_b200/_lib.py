@@ -77,8 +77,7 @@ SIGNATURES = {
     "hx_dist_destroy": (_I, [_P]),
     "hx_dist_buffer": (_P, [_P]),
     "hx_decode_attention_gather": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P,
-                                        C.c_size_t, _P, _I, _I, _I, _P, C.c_size_t, C.c_uint32,
-                                        _P]),
+                                        C.c_size_t, _P, _I, _I, _I, _P, C.c_size_t, _P]),
     "hx_dist_wait": (_I, [_P, C.c_uint32, _P]),
 }
 

@@ -62,9 +62,6 @@ struct DecodeParams {
     int out_row_limit;         // rows the destinations hold; a row beyond is skipped and recorded
     int out_vec;               // every destination is 16-byte aligned: rows go out as 16-byte stores
     int out_f32;
-    unsigned int* peer_flags[kHxMaxRanks];   // epoch words to post on the other ranks
-    int n_flags;
-    unsigned int epoch;
     float* ws_o;               // [slots][group][128]
     float2* ws_ml;             // [slots][group] (m, l)
     int* status;
@@ -213,22 +210,6 @@ __device__ __forceinline__ int64_t out_head_base(const DecodeParams& p, int s)
         return -1;
     }
     return (int64_t)row * p.out_hq + p.out_head0;
-}
-
-// Gathering calls post the call's epoch on every other rank once every row
-// this rank stored is performed system-wide.  post_epoch_kernel does it:
-// launched after the decode kernels as an ordinary stream launch, it starts
-// only when all of them have completed (their stores performed), then
-// fences at system scope and stores the epoch into each peer's flag word
-// with release semantics, so a rank that acquires the epoch also sees every
-// row this rank stored into its buffer.
-__global__ void post_epoch_kernel(const DecodeParams p)
-{
-    if (threadIdx.x != 0) return;
-    __threadfence_system();
-    for (int k = 0; k < p.n_flags; ++k)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[k]), "r"(p.epoch)
-                     : "memory");
 }
 
 // Stores n_rows finished rows (fp32 in shared memory, 128 dims each, row r
@@ -746,6 +727,10 @@ __global__ void __launch_bounds__(128)
     }
     __syncthreads();  // shared state is rewritten by the next item
     }
+    // CTA 0 always waits for the decode grid, so this grid never completes
+    // before it: a kernel launched after this one as a programmatic
+    // dependent then also waits for the decode kernel.
+    if (blockIdx.x == 0) pdl_wait();
 }
 
 // Any head_dim (<= 256), any group: one CTA of 4 warps per (sequence, q
@@ -976,16 +961,15 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
     return run_decode(c, p, workspace, (cudaStream_t)stream);
 }
 
-// Gathering decode: the rows go to every rank's buffer and the last CTA
-// posts the epoch (hx_dist state lives in dist.cu).
+// Gathering decode: the rows go to every rank's buffer (the endpoints and
+// the epoch exchange live in dist.cu).
 extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const void* q,
                                           int q_dtype, const int32_t* seq_ids,
                                           const int32_t* lengths, int n_seqs, int num_q_heads,
                                           float scale, hx_dist* dist, size_t out_offset,
                                           const int32_t* out_rows, int out_row_heads,
                                           int out_head0, int out_dtype, void* workspace,
-                                          size_t workspace_bytes, uint32_t epoch,
-                                          hx_stream_t stream)
+                                          size_t workspace_bytes, hx_stream_t stream)
 {
     if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
                                  out_dtype))
@@ -1021,22 +1005,14 @@ extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const
     p.out_hq = out_row_heads;
     p.out_head0 = out_head0;
     p.out_row_limit = rows > (size_t)INT32_MAX ? INT32_MAX : (int)rows;
-    p.n_flags = 0;
-    for (int r = 0; r < dist->world; ++r)
-        if (r != dist->rank) p.peer_flags[p.n_flags++] = dist->peer_flags[r] + dist->rank;
-    p.epoch = epoch;
     p.status = status_word();
     cudaStream_t s = (cudaStream_t)stream;
-    if (n_seqs > 0) {
-        const size_t need = needed_scratch(c, p);
-        if (need && (!workspace || workspace_bytes < need))
-            return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
-                        workspace_bytes, need);
-        if (int rc = run_decode(c, p, workspace, s)) return rc;
-    }
-    if (p.n_flags == 0) return HX_OK;
-    post_epoch_kernel<<<1, 32, 0, s>>>(p);
-    return check_launch("post_epoch_kernel");
+    if (n_seqs == 0) return HX_OK;
+    const size_t need = needed_scratch(c, p);
+    if (need && (!workspace || workspace_bytes < need))
+        return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
+                    workspace_bytes, need);
+    return run_decode(c, p, workspace, s);
 }
 
 // ---------------------------------------------------------------- no-allocation variant

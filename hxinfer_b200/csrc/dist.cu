@@ -4,9 +4,11 @@
 // block of flag words, [0, world) = the epoch each rank last posted here.
 // The region is exported with a CUDA IPC handle and mapped by every other
 // rank, so the decode kernels of rank r store rows straight into rank q's
-// buffer and then post their epoch into rank q's flags[r]
-// (decode_attention.cu: store_rows, post_epoch_kernel).  hx_dist_wait polls
-// the local flags with acquire loads at system scope.
+// buffer (decode_attention.cu: store_rows).  hx_dist_wait then runs one warp
+// after them on the stream: it fences at system scope, posts this rank's
+// epoch into every peer's flags[rank] with release stores, and polls the
+// local flags with acquire loads until every peer's epoch has arrived, so
+// rows a peer stored before its own post are visible here afterwards.
 //
 // The reference engine has no multi-GPU path (hxinfer-engine runs one
 // device); this replaces the NCCL all-gather a sharded decode would issue
@@ -37,14 +39,28 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const unsigned int* p)
     return v;
 }
 
-// One warp; lane r < world (r != rank) waits for flags[r] to reach `epoch`
-// (mod 2^32 comparison).  Bounded by kWaitTimeoutNs of %globaltimer.
-__global__ void dist_wait_kernel(const unsigned int* flags, int world, int rank, uint32_t epoch,
-                                 int* status)
+struct PeerFlags {
+    unsigned int* slot[kHxMaxRanks];  // peer r's flags[rank]; null for this rank
+};
+
+// One warp, launched as a programmatic dependent of the kernel before it on
+// the stream: it becomes resident early, and griddepcontrol.wait returns once
+// that kernel (and, through it, the decode kernels, whose last grid always
+// waits for its predecessor) has completed with its stores performed.  Then
+// lane r < world (r != rank) fences, posts `epoch` to peer r, and waits for
+// flags[r] to reach `epoch` (mod 2^32 comparison), bounded by
+// kWaitTimeoutNs of %globaltimer.
+__global__ void dist_wait_kernel(const unsigned int* flags, PeerFlags peers, int world, int rank,
+                                 uint32_t epoch, int* status)
 {
+    pdl_trigger();
+    pdl_wait();
     const int r = threadIdx.x;
     bool ok = true;
     if (r < world && r != rank) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.slot[r]), "r"(epoch)
+                     : "memory");
         const uint64_t t0 = globaltimer_ns();
         while ((int32_t)(ld_acquire_sys(flags + r) - epoch) < 0) {
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -163,7 +179,12 @@ extern "C" int hx_dist_wait(hx_dist* d, uint32_t epoch, hx_stream_t stream)
 {
     if (!d || !d->connected) return fail(HX_ERR_INVALID, "gather endpoint is not connected");
     if (d->world == 1) return HX_OK;
-    dist_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(d->flags, d->world, d->rank, epoch,
-                                                          status_word());
+    PeerFlags peers{};
+    for (int r = 0; r < d->world; ++r)
+        if (r != d->rank) peers.slot[r] = d->peer_flags[r] + d->rank;
+    cudaError_t e = launch_kernel(dist_wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream,
+                                  true, (const unsigned int*)d->flags, peers, d->world, d->rank,
+                                  epoch, status_word());
+    if (e != cudaSuccess) return cuda_fail(e, "dist_wait_kernel launch");
     return check_launch("dist_wait_kernel");
 }

@@ -200,14 +200,15 @@ class KVCache:
     def decode_gather(self, layer: int, q: torch.Tensor, seq_ids: torch.Tensor,
                       lengths: torch.Tensor, num_q_heads: int, gather: "PeerGather", *,
                       out_offset: int, out_rows: torch.Tensor, out_row_heads: int,
-                      out_head0: int, epoch: int, scale: float | None = None,
+                      out_head0: int, scale: float | None = None,
                       out_dtype=torch.float16, workspace: torch.Tensor | None = None,
                       stream=None):
         """Decode attention of this rank's shard with the outputs stored into
         every rank's gather buffer (hx_decode_attention_gather): q head qh of
         local sequence s lands in row out_rows[s], column block out_head0+qh,
         of the [rows][out_row_heads*head_dim] matrix at byte out_offset.
-        Follow it by ``gather.wait(epoch)`` before reading the buffer."""
+        Follow it by ``gather.wait(epoch)`` (on every rank) before reading
+        the buffer."""
         _need_cuda(q, seq_ids, lengths, out_rows, workspace)
         n = seq_ids.numel()
         if scale is None:
@@ -219,8 +220,8 @@ class KVCache:
         check(load().hx_decode_attention_gather(
             self.handle, layer, _ptr(q), _dt(q), _ptr(seq_ids), _ptr(lengths), n, num_q_heads,
             scale, gather.handle, out_offset, _ptr(out_rows), out_row_heads, out_head0, odt,
-            _ptr(workspace), workspace.numel() * workspace.element_size(), epoch & 0xFFFFFFFF,
-            _stream(stream)), "decode attention (gather)")
+            _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
+            "decode attention (gather)")
 
     def prefill(self, layer: int, q: torch.Tensor, seq: int, start: int, num_q_heads: int, *,
                 scale: float | None = None, out: torch.Tensor | None = None,
@@ -291,6 +292,9 @@ class PeerGather:
             *(shape if shape is not None else (numel,)))
 
     def wait(self, epoch: int, stream=None):
+        """Posts `epoch` to every other rank once the work before it on the
+        stream has completed, and holds the stream until every other rank has
+        posted it (hx_dist_wait)."""
         check(load().hx_dist_wait(self.handle, epoch & 0xFFFFFFFF, _stream(stream)), "dist wait")
 
     def close(self):

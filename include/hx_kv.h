@@ -234,10 +234,9 @@ int hx_decode_attention_noalloc(const hx_kv_cache* cache, int layer, const void*
  * GPU), with the all-gather of the per-rank outputs fused into the decode
  * kernels.  Each rank owns a gather buffer; the decode and combine kernels
  * store every output row of this rank into every rank's buffer over NVLink
- * peer memory (16-byte stores, no bulk copy), and a one-thread kernel
- * launched after them posts the call's epoch into a flag word on every other
- * rank.  hx_dist_wait then holds the stream until every other rank's epoch
- * has arrived.  The
+ * peer memory (16-byte stores, no bulk copy).  hx_dist_wait then posts this
+ * rank's epoch into a flag word on every other rank and holds the stream
+ * until every other rank's epoch has arrived.  The
  * reference engine is single-GPU; this replaces an NCCL all-gather issued
  * after each decode call.
  *
@@ -267,12 +266,10 @@ void* hx_dist_buffer(const hx_dist* dist);
 
 /* hx_decode_attention for this rank's shard, with the outputs written into
  * every rank's gather buffer.  The output is a matrix starting at byte
- * out_offset of each buffer, [rows][out_row_heads*128] in out_dtype: q head
- * qh of local sequence s goes to row out_rows[s] (device int32 [n_seqs]),
- * column block out_head0 + qh.  The ranks' (row, column) blocks must not
- * overlap.  epoch: a value greater (mod 2^32) than that of this endpoint's
- * previous call, the same on every rank for the same step.  Every rank makes
- * the same sequence of calls (also with n_seqs == 0, which only signals).
+ * out_offset (a multiple of 16) of each buffer, [rows][out_row_heads*128] in
+ * out_dtype: q head qh of local sequence s goes to row out_rows[s] (device
+ * int32 [n_seqs]), column block out_head0 + qh.  The ranks' (row, column)
+ * blocks must not overlap.  n_seqs may be 0 (nothing is written).
  *
  * The call does not wait for the other ranks: follow it by hx_dist_wait
  * before reading the buffer.  A region of the buffer may be written again
@@ -283,11 +280,15 @@ int hx_decode_attention_gather(const hx_kv_cache* cache, int layer, const void* 
                                int num_q_heads, float scale, hx_dist* dist, size_t out_offset,
                                const int32_t* out_rows, int out_row_heads, int out_head0,
                                int out_dtype, void* workspace, size_t workspace_bytes,
-                               uint32_t epoch, hx_stream_t stream);
-/* Holds `stream` until every other rank has posted `epoch` (a one-CTA kernel
- * polling this rank's flag words).  The wait is bounded (4 s); when it runs
- * out the kernel records HX_ERR_TIMEOUT in the device status word and
- * returns, so the host finds the failure through hx_device_status. */
+                               hx_stream_t stream);
+/* Exchanges `epoch` with every other rank: once everything launched before
+ * it on `stream` has completed, posts `epoch` to every other rank and holds
+ * the stream until every other rank has posted it here (one warp; rows a
+ * rank stored before its post are then visible).  Every rank calls it with
+ * the same epoch, greater (mod 2^32) than its previous one, after the same
+ * gathering calls.  The wait is bounded (4 s); when it runs out the kernel
+ * records HX_ERR_TIMEOUT in the device status word and returns, so the host
+ * finds the failure through hx_device_status. */
 int hx_dist_wait(hx_dist* dist, uint32_t epoch, hx_stream_t stream);
 
 /* ------------------------------------------------------------ prefix snapshots */

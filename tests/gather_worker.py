@@ -93,7 +93,7 @@ def run_case(rank, world, dev, name, hq, hkv, lengths, out_dtype):
             epoch += 1
             cache.decode_gather(l, q_loc[l], sid, lens, len(qh), peer, out_offset=l * layer_bytes,
                                 out_rows=rows, out_row_heads=hq, out_head0=heads[0] * group,
-                                epoch=epoch, out_dtype=out_dtype, workspace=ws)
+                                out_dtype=out_dtype, workspace=ws)
             peer.wait(epoch)
             if step == 0:
                 plain.append(cache.decode(l, q_loc[l], sid, lens, len(qh), out_dtype=out_dtype)
