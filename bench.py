@@ -212,7 +212,7 @@ def run_batched_decode(args):
     my_len = np.array([int(lengths[s]) for s in seqs], np.int64)
     cap = int(my_len.max()) + extra
     nblocks = int(sum(math.ceil((int(L) + extra) / 64) for L in my_len))
-    cache = kv.KVCache(LAYERS, hkv, HD, n, cap, num_blocks=nblocks)
+    cache = kv.KVCache(LAYERS, hkv, HD, n, cap, num_blocks=nblocks, overlap=args.overlap)
     for i, L in enumerate(my_len):
         cache.reserve(i, int(L) + extra)
     cache.fill_normal(SEED + 1000 * rank)
@@ -429,6 +429,8 @@ def main():
     ap.add_argument("--workload", default="batched_decode",
                     choices=["batched_decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--overlap", action="store_true",
+                    help="launch append and decode as programmatic dependents (HX_KV_OVERLAP_LAUNCH)")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: gather fused into the decode kernels over NVLink peer memory "
                          "(p2p) or an NCCL all-gather after each decode call (nccl)")

@@ -610,9 +610,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 // has finished.  Segments that one CTA covered were already written by the
 // decode kernel.  The pieces are slot `seg` (the one starting at the
 // segment's first tile) then slot n_seg + c for each CTA c whose non-empty
-// range starts inside the segment, merged in that fixed order: warp 0 loads
-// every piece's (m, l) in one round and leaves normalised weights in shared
-// memory; each thread then loads its dim of every piece in one round.
+// range starts inside the segment.  The four warps split the pieces and
+// merge their share online (one round of loads per 32 pieces); the warps'
+// results are then merged in shared memory.
 //
 // Items (segment, q row) are numbered seg * group + r; CTA b takes items b,
 // b + gridDim.x, ...; the launch gives one CTA per item, since each item is
@@ -626,7 +626,8 @@ __global__ void __launch_bounds__(128)
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     __shared__ int sh_range[4];  // a, b, T, n_eff
     __shared__ int slot_list[kMaxPieces];
-    __shared__ float weights[kMaxPieces];
+    __shared__ float w_m[4], w_l[4];
+    __shared__ __align__(16) float w_acc[4][128];
     __shared__ __align__(16) float row_buf[128];
     __shared__ int sh_np;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -674,54 +675,76 @@ __global__ void __launch_bounds__(128)
     }
     __syncthreads();
     const int np = sh_np;  // <= 1: the decode kernel wrote this output itself
-    if (np > 1) pdl_wait();  // the pieces come from the decode grid
-    if (np > 1 && warp == 0) {
-        constexpr int kPerLane = (kMaxPieces + 31) / 32;
-        float2 ml[kPerLane];
+    if (np > 1) {
+        pdl_wait();  // the pieces come from the decode grid
+        // Warp w merges pieces w, w + 4, ... (online, in groups of 32): lane
+        // i holds one piece's (m, l); each lane accumulates dims 4*lane..+3
+        // of every piece's O.  All loads of a group are independent, so a
+        // group costs one round of L2 latency.
+        const int n_w = np > warp ? (np - warp + 3) / 4 : 0;
+        float Mw = -INFINITY, Lw = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        constexpr int kSub = 8;  // O loads in flight per lane
+        for (int base = 0; base < n_w; base += 32) {
+            const int cnt = min(32, n_w - base);
+            const float2 ml = lane < cnt
+                ? __ldcg(&p.ws_ml[(int64_t)slot_list[warp + 4 * (base + lane)] * p.group + r])
+                : make_float2(-INFINITY, 0.f);
+            float4 ov[kSub];
 #pragma unroll
-        for (int u = 0; u < kPerLane; ++u) {
-            const int q = lane + 32 * u;
-            ml[u] = q < np ? __ldcg(&p.ws_ml[(int64_t)slot_list[q] * p.group + r])
-                           : make_float2(-INFINITY, 0.f);
+            for (int j = 0; j < kSub; ++j)
+                ov[j] = j < cnt ? __ldcg(reinterpret_cast<const float4*>(
+                                      p.ws_o + ((int64_t)slot_list[warp + 4 * (base + j)] * p.group + r) * 128) + lane)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            float Mc = ml.x;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, o));
+            const float Mn = fmaxf(Mw, Mc);
+            const float Mu = Mn == -INFINITY ? 0.f : Mn;
+            const float sc = fast_exp2(Mw - Mu);  // 0 while nothing is merged
+            acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+            const float wl = fast_exp2(ml.x - Mu);  // 0 for lanes without a piece
+            float lsum = wl * ml.y;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            Lw = Lw * sc + lsum;
+            Mw = Mn;
+            for (int j0 = 0; j0 < cnt; j0 += kSub) {
+                if (j0 > 0) {
+#pragma unroll
+                    for (int j = 0; j < kSub; ++j)
+                        ov[j] = j0 + j < cnt ? __ldcg(reinterpret_cast<const float4*>(
+                                                   p.ws_o + ((int64_t)slot_list[warp + 4 * (base + j0 + j)] * p.group + r) * 128) + lane)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kSub; ++j) {
+                    const float wj = __shfl_sync(0xffffffffu, wl, (j0 + j) & 31);
+                    if (j0 + j < cnt) {
+                        acc.x += wj * ov[j].x; acc.y += wj * ov[j].y;
+                        acc.z += wj * ov[j].z; acc.w += wj * ov[j].w;
+                    }
+                }
+            }
         }
+        if (lane == 0) {
+            w_m[warp] = Mw;
+            w_l[warp] = Lw;
+        }
+        *reinterpret_cast<float4*>(&w_acc[warp][4 * lane]) = acc;
+        __syncthreads();
         float M = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < kPerLane; ++u) M = fmaxf(M, ml[u].x);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, w_m[w]);
         const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, w[kPerLane];
+        float num = 0.f, den = 0.f;
 #pragma unroll
-        for (int u = 0; u < kPerLane; ++u) {
-            w[u] = fast_exp2(ml[u].x - Mu);
-            L += w[u] * ml[u].y;
+        for (int w = 0; w < 4; ++w) {
+            const float f = fast_exp2(w_m[w] - Mu);
+            num += f * w_acc[w][t];
+            den += f * w_l[w];
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float inv = 1.f / L;
-#pragma unroll
-        for (int u = 0; u < kPerLane; ++u) {
-            const int q = lane + 32 * u;
-            if (q < np) weights[q] = w[u] * inv;
-        }
-    }
-    // each thread's loads do not depend on the weights: issue them first
-    constexpr int kBatch = 32;
-    float acc = 0.f;
-    for (int q0 = 0; q0 < np; q0 += kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int q = q0 + u;
-            v[u] = q < np ? __ldcg(p.ws_o + ((int64_t)slot_list[q] * p.group + r) * 128 + t) : 0.f;
-        }
-        __syncthreads();  // weights ready (first batch); harmless afterwards
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u)
-            if (q0 + u < np) acc += weights[q0 + u] * v[u];
-    }
-    if (np > 1) {
-        row_buf[t] = acc;
+        row_buf[t] = num / den;
         __syncthreads();
         store_rows(p, s, h * p.group + r, row_buf, 128, 1, t, 128);
     }
