@@ -46,6 +46,12 @@ sys.path.insert(0, ROOT)
 
 SEED = 20261201
 HQ, HKV, HD, LAYERS, NSEQ = 32, 8, 128, 32, 64
+# DRAM bytes (read + write) of one decode launch / its algorithmic bytes,
+# from an ncu capture of the same kernel on 16 sequences x 8192 positions
+# (540.6 MB of DRAM traffic for 537.0 MB of K+V+q+out); the traffic of the
+# bench's 4.4 GB launches scales with the tiles read, so `roofline.traffic`
+# is this ratio times the launch's algorithmic bytes.
+DECODE_TRAFFIC_RATIO = 1.007
 
 
 def lengths_c4():
@@ -399,7 +405,9 @@ def run_batched_decode(args):
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "decode_attention_kernel + decode_combine_kernel (one call)",
                          "bytes_per_launch": dec_bytes, "avg_launch_ms": dec_avg_ms,
-                         "traffic": None},
+                         "traffic": DECODE_TRAFFIC_RATIO * dec_bytes,
+                         "traffic_source": "ncu dram__bytes_read+write, 16x8192 capture, "
+                                           "scaled by tiles read"},
             "hbm_gbs_step": float(2 * (lengths.sum() + NSEQ) * HKV * HD * 2 * LAYERS) / (ms / K * 1e-3) / 1e9,
             "cpu_baseline": cpu,
             "e2e": {"value": NSEQ * K / (e2e_ms * 1e-3), "unit": "tok/s",
