@@ -4,6 +4,7 @@
     python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
+    python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
 
 Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
 prints one JSON line with the CUDA-event time per iteration and the
@@ -142,20 +143,99 @@ def prefill_case(a):
                       "tflops": flops / (avg * 1e-3) / 1e12}))
 
 
+def c2_case(a):
+    """LLaMA-2-7B MHA shape (32 q = 32 kv heads, theta 1e4), batch 1: K1 appends
+    a 1024-token prompt, K3 prefills it, then 1024 decode steps each append one
+    token (K1) and attend over the grown cache (K2).  The decode steps are
+    captured once in a CUDA graph (every step's positions baked in) and timed
+    as replays, so host launch time is not counted."""
+    hq = hkv = 32
+    hd, n0, steps, layers = 128, a.len, a.steps, a.layers
+    cap = n0 + steps
+    cache = kv.KVCache(layers, hkv, hd, 1, cap)
+    cache.reserve(0, cap)
+    table = kv.RopeTable(hd, cap, 1e4)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    dev = torch.device("cuda")
+    qp = torch.randn((n0, hq * hd), generator=g, device=dev).half()
+    kp = torch.randn((n0, hkv * hd), generator=g, device=dev).half()
+    vp = torch.randn((n0, hkv * hd), generator=g, device=dev).half()
+    qd = torch.randn((steps, 1, hq * hd), generator=g, device=dev).half()
+    kd = torch.randn((steps, 1, hkv * hd), generator=g, device=dev).half()
+    vd = torch.randn((steps, 1, hkv * hd), generator=g, device=dev).half()
+    q_rot = torch.empty_like(qp)
+    qd_rot = torch.empty_like(qd)
+    out_p = torch.empty_like(qp)
+    out_d = torch.empty_like(qd)
+    sid0 = torch.zeros(n0, dtype=torch.int32, device=dev)
+    pos0 = torch.arange(n0, dtype=torch.int32, device=dev)
+    sid = torch.zeros(1, dtype=torch.int32, device=dev)
+    pos_tab = torch.arange(n0, n0 + steps, dtype=torch.int32, device=dev).view(steps, 1)
+    len_tab = pos_tab + 1
+    ws = torch.zeros(cache.workspace_bytes(1, hq), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream()
+
+    def prefill():
+        for l in range(layers):
+            cache.rope_append(l, kp, vp, sid0, pos0, q=qp, num_q_heads=hq, table=table,
+                              q_out=q_rot, stream=stream)
+            cache.prefill(l, q_rot, 0, 0, hq, out=out_p, stream=stream)
+
+    def decode_all():
+        for t in range(steps):
+            for l in range(layers):
+                cache.rope_append(l, kd[t], vd[t], sid, pos_tab[t], q=qd[t], num_q_heads=hq,
+                                  table=table, q_out=qd_rot[t], stream=stream)
+                cache.decode(l, qd_rot[t], sid, len_tab[t], hq, out=out_d[t], workspace=ws,
+                             stream=stream)
+
+    with torch.cuda.stream(stream):
+        prefill()
+        decode_all()  # warm-up, sets kernel attributes outside capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            decode_all()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record(stream)
+        prefill()
+        e[1].record(stream)
+        graph.replay()
+        e[2].record(stream)
+        graph.replay()
+        e[3].record(stream)
+        torch.cuda.synchronize()
+    kv.device_status()
+    pre_ms = e[0].elapsed_time(e[1])
+    dec_ms = e[2].elapsed_time(e[3])
+    pairs = n0 * (n0 + 1) // 2
+    pre_flops = 4.0 * hq * hd * pairs * layers
+    dec_bytes = 2.0 * hkv * hd * 2 * sum(range(n0 + 1, n0 + steps + 1)) * layers
+    print(json.dumps({"case": "c2", "shape": "llama2", "prompt": n0, "decode_steps": steps,
+                      "layers": layers, "prefill_ms": pre_ms,
+                      "prefill_tflops_incl_append": pre_flops / (pre_ms * 1e-3) / 1e12,
+                      "decode_ms": dec_ms, "decode_us_per_step_layer": 1e3 * dec_ms / (steps * layers),
+                      "decode_kv_bytes": dec_bytes,
+                      "decode_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot", "prefill"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2"])
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
     ap.add_argument("--len", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--start", type=int, default=0)
+    ap.add_argument("--steps", type=int, default=1024, help="c2: decode steps after the prompt")
     ap.add_argument("--overlap", action="store_true",
                     help="programmatic dependent launch of append -> decode (HX_KV_OVERLAP_LAUNCH)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case}[a.case](a)
+    {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case,
+     "c2": c2_case}[a.case](a)
 
 
 if __name__ == "__main__":

@@ -58,3 +58,24 @@ def test_null_arguments_are_rejected_without_a_device(hxlib):
     assert hxlib.hx_kv_create(C.byref(bad), C.byref(out)) == _lib.HX_ERR_INVALID
     assert hxlib.hx_decode_workspace_bytes(None, 1, 1) == 0
     assert hxlib.hx_snapshot_bytes(None, 4) == 0
+
+
+def test_gather_endpoint_arguments_are_checked_without_a_device(hxlib):
+    """The multi-GPU endpoint validates rank/world/sizes before any CUDA call,
+    and the gathering decode refuses an unconnected endpoint."""
+    import ctypes as C
+    from hxinfer_b200 import _lib
+    assert 0 < hxlib.hx_dist_handle_bytes() <= 128
+    out = C.c_void_p()
+    for rank, world, nbytes in ((0, 0, 64), (0, 9, 64), (2, 2, 64), (-1, 2, 64), (0, 2, 0)):
+        assert hxlib.hx_dist_create(rank, world, nbytes, C.byref(out)) == _lib.HX_ERR_INVALID
+        assert not out.value
+    assert hxlib.hx_dist_create(0, 2, 64, None) == _lib.HX_ERR_INVALID
+    assert hxlib.hx_dist_export(None, None) == _lib.HX_ERR_INVALID
+    assert hxlib.hx_dist_connect(None, None) == _lib.HX_ERR_INVALID
+    assert hxlib.hx_dist_wait(None, 1, None) == _lib.HX_ERR_INVALID
+    assert hxlib.hx_dist_destroy(None) == _lib.HX_OK
+    assert hxlib.hx_dist_buffer(None) is None
+    assert hxlib.hx_decode_attention_gather(None, 0, None, _lib.HX_FP16, None, None, 0, 1, 1.0,
+                                            None, 0, None, 1, 0, _lib.HX_FP16, None, 0,
+                                            None) == _lib.HX_ERR_INVALID
