@@ -7,21 +7,27 @@
 // positions) and re-reads K/V once per q head.  Here:
 //
 //  * Work is the flat list of 64-position tiles over all (sequence, kv head)
-//    segments; CTA c of C (one per SM) takes tiles [c*T/C, (c+1)*T/C), so
-//    every CTA streams the same number of bytes whatever the lengths.
+//    segments; CTA c of C takes tiles [c*T/C, (c+1)*T/C), so every CTA
+//    streams the same number of bytes whatever the lengths.  C is one CTA
+//    per SM (6-stage ring) or, for calls with many segments, two CTAs per SM
+//    (3-stage rings) so that one CTA's tail overlaps the other's streaming.
 //  * Warp 4 (producer) streams each tile's K and V (2 x 16 KiB) with TMA
 //    (cp.async.bulk.tensor, 64x64 boxes, 128-byte swizzle, L2 evict-first)
-//    into a 6-stage mbarrier ring; no multicast.
-//  * Warps 0-3 (consumers) each own 16 positions of every tile.  The whole
-//    GQA group of q heads is packed into the rows of one mma.sync
-//    m16n8k16 tile, so each K/V tile is read from HBM once per group; scores
-//    and P.V accumulate in fp32; the softmax is online (running max and sum
-//    per row, warp-shuffle reductions inside each quad).
+//    into the mbarrier ring; no multicast.
+//  * Warps 0-3 (consumers) each own 16 positions of every tile.  The MMAs
+//    (mma.sync m16n8k16, fp16 in, fp32 accumulate) run transposed: the
+//    warp's positions are the M side and the GQA group's q rows the N side
+//    (8 rows per n-tile), so each K/V tile is read from HBM once per group
+//    and a group of up to 8 rows needs no padding: S^T = K Q^T, then
+//    O^T += V^T P^T with P^T moved into operand layout by movmatrix.  The
+//    softmax is online (running max and sum per row, warp-shuffle reductions
+//    over the lanes that share a row).
 //  * At the end of each piece (the part of a segment inside one CTA) the four
-//    warps merge in shared memory.  A piece that is a whole segment writes
-//    the normalised output; otherwise it writes (O, m, l) to a workspace slot
-//    and decode_combine_kernel (one CTA per segment and q row, launched as a
-//    programmatic dependent) merges the pieces by log-sum-exp.
+//    warps merge in the shared memory of the stage they just consumed.  A
+//    piece that is a whole segment writes the normalised output; otherwise
+//    it writes (O, m, l) to a workspace slot and decode_combine_kernel (one
+//    CTA per segment and q row, launched as a programmatic dependent) merges
+//    the pieces by log-sum-exp.
 //
 // Workspace: slot (seq*hkv + kv_head) holds the piece that starts at a
 // segment's first tile; slot (n_segments + c) holds CTA c's first piece when
@@ -34,13 +40,22 @@
 
 namespace hx {
 
-constexpr int kDecStages = 6;
+// Two launch shapes of the same kernel:
+//  * narrow: one CTA per SM with a 6-stage ring;
+//  * wide: two CTAs per SM, each with a 3-stage ring (the same bytes in
+//    flight per SM), so one CTA's end-of-range merge, its exit and the next
+//    CTA's start overlap the other CTA's streaming.  It needs the 8-row GQA
+//    tile (the 16-row one has too many registers for two CTAs) and pays off
+//    when every CTA has many tiles; with few segments (batch-1 long context)
+//    its shorter ring loses, so calls with fewer than kWideMinSegments
+//    (sequence, kv head) segments use the narrow shape.
+constexpr int kWideMinSegments = 64;
 constexpr int kDecConsumerWarps = 4;
 constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kHalfTileBytes = 64 * 64 * 2;       // one 64x64 fp16 TMA box
 constexpr int kTileBytes = 2 * kHalfTileBytes;     // 64 positions x 128 dims
 constexpr uint32_t kStageTxBytes = 2 * kTileBytes; // K + V
-constexpr int kMaxPieces = 224;  // bound on split-K pieces per segment (needs C + 2 <= it)
+constexpr int kMaxPieces = 300;  // bound on split-K pieces per segment (needs C + 2 <= it)
 
 struct DecodeParams {
     KVView view;
@@ -78,14 +93,16 @@ struct Sched {
     int n_eff;                     // CTAs that received work
 };
 
-template <int ROWS>
+template <int ROWS, int STAGES>
 struct DecodeSmem {
-    uint8_t stage[kDecStages][2][kTileBytes];  // [stage][K|V]: two 64x64 boxes each
-    float merge_o[kDecConsumerWarps][ROWS][128];
+    // [stage][K|V]: two 64x64 boxes each.  At the end of a piece the stage
+    // just consumed also holds the warps' O partials (merge_o), before it is
+    // released to the producer.
+    uint8_t stage[STAGES][2][kTileBytes];
     float merge_m[kDecConsumerWarps][ROWS];
     float merge_l[kDecConsumerWarps][ROWS];
-    uint64_t full[kDecStages];
-    uint64_t empty[kDecStages];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
     Sched sched;
     int cstart[kMaxPieces];    // first global tile of CTA c, c in [0, n_eff]
 };
@@ -123,8 +140,8 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p)
 // get work (n_eff = min(grid, ceil(T / kMinTilesPerCta))), every CTA's first
 // tile (cstart, so later piece arithmetic is a shared-memory lookup), and
 // this CTA's starting cursor.
-template <int ROWS>
-__device__ void plan_cta(const DecodeParams& p, int cta, int grid, DecodeSmem<ROWS>& sm)
+template <typename Smem>
+__device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
 {
     const int lane = threadIdx.x & 31;
     const int hkv = p.view.hkv;
@@ -275,13 +292,14 @@ __device__ void zero_empty_outputs(const DecodeParams& p)
     }
 }
 
-template <int ROWS>
-__global__ void __launch_bounds__(kDecThreads, 1)
+template <int ROWS, int STAGES, int CTAS_PER_SM>
+__global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const DecodeParams p)
 {
+    constexpr int kDecStages = STAGES;
     extern __shared__ uint8_t smem_raw[];
-    auto& sm = *reinterpret_cast<DecodeSmem<ROWS>*>(
+    auto& sm = *reinterpret_cast<DecodeSmem<ROWS, STAGES>*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x, n_ctas = gridDim.x;
@@ -365,9 +383,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     pdl_wait();  // q and the newest cache position come from the previous kernel
     const int g = lane >> 2, t4 = lane & 3;
     const int w = warp;
-    uint32_t qa[8][4];
-    float o[16][4];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    // The MMAs run transposed: positions are the M side (16 per warp) and the
+    // GQA group's q rows the N side, in NT n-tiles of 8 rows, so a group of up
+    // to 8 rows needs no padding.  S^T = K Q^T, then O^T += V^T P^T.
+    constexpr int NT = ROWS / 8;
+    uint32_t qb[NT][8][2];  // B operand: q row 8nt+g, dims 16kk+2t4 (+8)
+    float o[NT][8][4];      // O^T: dims 16mt+g (+8) x rows 8nt+2t4 (+1)
+    float mrow[NT][2], lrow[NT][2];  // rows 8nt+2t4+c: running max, this lane's partial sum
     bool piece_from_seg_start = false;
     bool dead = false;  // a bounded wait ran out
     const uint32_t stage_base = smem_u32(&sm.stage[0][0][0]);
@@ -380,14 +402,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             piece_from_seg_start = (cur.j == 0);
             const int64_t qrow0 = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group) * 128;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
+            for (int nt = 0; nt < NT; ++nt) {
+                const int r = 8 * nt + g;
 #pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {  // row g (hi=0) or g+8 (hi=1)
-                    const int r = g + 8 * hi;
+                for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {  // dims 16kk+2t4 (+8)
                         uint32_t val = 0;
-                        if (r < p.group && (hi == 0 || ROWS == 16)) {
+                        if (r < p.group) {
                             const int64_t idx = qrow0 + (int64_t)r * 128 + 16 * kk + 2 * t4 + 8 * half;
                             if (p.q_f32) {
                                 const float2 f = *reinterpret_cast<const float2*>(
@@ -398,14 +420,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                                     static_cast<const __half*>(p.q) + idx);
                             }
                         }
-                        qa[kk][hi + 2 * half] = val;
+                        qb[nt][kk][half] = val;
                     }
                 }
-            }
 #pragma unroll
-            for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-            m0 = m1 = -INFINITY;
-            l0 = l1 = 0.f;
+                for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+                mrow[nt][0] = mrow[nt][1] = -INFINITY;
+                lrow[nt][0] = lrow[nt][1] = 0.f;
+            }
         }
 
         const int st = i % kDecStages;
@@ -440,9 +462,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             __syncwarp();
         }
 
-        // S = Q K^T for this warp's 16 positions (two n-tiles of 8)
-        float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        float sb[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // S^T = K Q^T for this warp's 16 positions (two accumulator chains)
+        float sa[NT][4], sb[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
         {
             const int tok = tok0 + 8 * (lm_mi >> 1) + lm_r;
 #pragma unroll
@@ -450,117 +475,95 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 const int chunk = 2 * kk + (lm_mi & 1);
                 const uint32_t addr = kb + (chunk >> 3) * kHalfTileBytes + tok * 128 +
                                       (((chunk & 7) ^ (tok & 7)) << 4);
-                uint32_t b00, b01, b10, b11;
-                ldmatrix_x4(b00, b01, b10, b11, addr);
-                if (kk & 1) {
-                    mma_16816(sb[0], qa[kk], b00, b01);
-                    mma_16816(sb[1], qa[kk], b10, b11);
-                } else {
-                    mma_16816(sa[0], qa[kk], b00, b01);
-                    mma_16816(sa[1], qa[kk], b10, b11);
+                uint32_t r0, r1, r2, r3;
+                ldmatrix_x4(r0, r1, r2, r3, addr);
+                const uint32_t a[4] = {r0, r2, r1, r3};  // positions x dims fragment
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    if (kk & 1) mma_16816(sb[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
+                    else mma_16816(sa[nt], a, qb[nt][kk][0], qb[nt][kk][1]);
                 }
             }
         }
-        float s[2][4];
+        // online softmax per q row; this lane holds rows 8nt+2t4+c at positions
+        // tok0+g (element c) and tok0+g+8 (element c+2); a row's max is
+        // reduced over the eight lanes that share t4
+        uint32_t pb[NT][2];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int nt = 0; nt < NT; ++nt) {
+            float pr[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int tok = tok0 + 8 * nt + 2 * t4 + (e & 1);
-                const float x = (sa[nt][e] + sb[nt][e]) * p.scale_log2;
-                s[nt][e] = tok < valid ? x : -INFINITY;
+            for (int c = 0; c < 2; ++c) {
+                const float x0 = (sa[nt][c] + sb[nt][c]) * p.scale_log2;
+                const float x1 = (sa[nt][c + 2] + sb[nt][c + 2]) * p.scale_log2;
+                const float s0 = tok0 + g < valid ? x0 : -INFINITY;
+                const float s1 = tok0 + g + 8 < valid ? x1 : -INFINITY;
+                float mx = fmaxf(s0, s1);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(mrow[nt][c], mx);
+                const float mu = mn == -INFINITY ? 0.f : mn;
+                const float al = fast_exp2(mrow[nt][c] - mu);
+                pr[c] = fast_exp2(s0 - mu);
+                pr[c + 2] = fast_exp2(s1 - mu);
+                lrow[nt][c] = lrow[nt][c] * al + (pr[c] + pr[c + 2]);
+                mrow[nt][c] = mn;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    o[nt][mt][c] *= al;
+                    o[nt][mt][c + 2] *= al;
+                }
             }
-
-        // online softmax, row g (elements 0,1) and row g+8 (elements 2,3)
-        float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        const float mn0 = fmaxf(m0, mx0);
-        const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-        const float al0 = fast_exp2(m0 - mu0);
-        float pr[2][4];
-        pr[0][0] = fast_exp2(s[0][0] - mu0);
-        pr[0][1] = fast_exp2(s[0][1] - mu0);
-        pr[1][0] = fast_exp2(s[1][0] - mu0);
-        pr[1][1] = fast_exp2(s[1][1] - mu0);
-        l0 = l0 * al0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
-        m0 = mn0;
-        float al1 = 1.f;
-        if (ROWS == 16) {
-            float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-            const float mn1 = fmaxf(m1, mx1);
-            const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-            al1 = fast_exp2(m1 - mu1);
-            pr[0][2] = fast_exp2(s[0][2] - mu1);
-            pr[0][3] = fast_exp2(s[0][3] - mu1);
-            pr[1][2] = fast_exp2(s[1][2] - mu1);
-            pr[1][3] = fast_exp2(s[1][3] - mu1);
-            l1 = l1 * al1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
-            m1 = mn1;
-        } else {
-            pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.f;
+            // P^T as the B operand of the P.V step: transpose the two 8x8
+            // (positions x rows) halves in registers
+            pb[nt][0] = movmatrix_trans(pack_half2(pr[0], pr[1]));
+            pb[nt][1] = movmatrix_trans(pack_half2(pr[2], pr[3]));
         }
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-            o[n][0] *= al0;
-            o[n][1] *= al0;
-            if (ROWS == 16) {
-                o[n][2] *= al1;
-                o[n][3] *= al1;
-            }
-        }
-        uint32_t pa[4];
-        pa[0] = pack_half2(pr[0][0], pr[0][1]);
-        pa[1] = pack_half2(pr[0][2], pr[0][3]);
-        pa[2] = pack_half2(pr[1][0], pr[1][1]);
-        pa[3] = pack_half2(pr[1][2], pr[1][3]);
 
-        // O += P V over this warp's 16 positions, 16 n-tiles of 8 dims
+        // O^T += V^T P^T over this warp's 16 positions, 8 m-tiles of 16 dims
         {
-            const int tok = tok0 + 8 * (lm_mi & 1) + lm_r;
+            const int tok = tok0 + 8 * (lm_mi >> 1) + lm_r;
 #pragma unroll
-            for (int np = 0; np < 8; ++np) {
-                const int chunk = 2 * np + (lm_mi >> 1);
+            for (int mt = 0; mt < 8; ++mt) {
+                const int chunk = 2 * mt + (lm_mi & 1);
                 const uint32_t addr = vb + (chunk >> 3) * kHalfTileBytes + tok * 128 +
                                       (((chunk & 7) ^ (tok & 7)) << 4);
-                uint32_t v0, v1, v2, v3;
-                ldmatrix_x4_trans(v0, v1, v2, v3, addr);
-                mma_16816(o[2 * np], pa, v0, v1);
-                mma_16816(o[2 * np + 1], pa, v2, v3);
+                uint32_t a[4];
+                ldmatrix_x4_trans(a[0], a[1], a[2], a[3], addr);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma_16816(o[nt][mt], a, pb[nt][0], pb[nt][1]);
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[st]);
-
         const bool seg_end = (cur.j == cur.tiles - 1);
-        if (seg_end || i == count - 1) {
-            // ---- merge the four warps' partials of this piece
-            float lq0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
-            lq0 += __shfl_xor_sync(0xffffffffu, lq0, 2);
-            float lq1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
-            lq1 += __shfl_xor_sync(0xffffffffu, lq1, 2);
-            if (g < p.group) {
-                if (t4 == 0) {
-                    sm.merge_m[w][g] = m0;
-                    sm.merge_l[w][g] = lq0;
-                }
+        const bool piece_end = seg_end || i == count - 1;
+        if (!piece_end && lane == 0) mbar_arrive(&sm.empty[st]);
+        if (piece_end) {
+            // ---- merge the four warps' partials of this piece, in the stage
+            // just consumed (released only once the merge is done)
+            auto merge_o = reinterpret_cast<float (*)[ROWS][128]>(&sm.stage[st][0][0]);
+            asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");  // stage read by all
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    sm.merge_o[w][g][8 * n + 2 * t4] = o[n][0];
-                    sm.merge_o[w][g][8 * n + 2 * t4 + 1] = o[n][1];
-                }
-            }
-            if (ROWS == 16 && g + 8 < p.group) {
-                if (t4 == 0) {
-                    sm.merge_m[w][g + 8] = m1;
-                    sm.merge_l[w][g + 8] = lq1;
-                }
+            for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    sm.merge_o[w][g + 8][8 * n + 2 * t4] = o[n][2];
-                    sm.merge_o[w][g + 8][8 * n + 2 * t4 + 1] = o[n][3];
+                for (int c = 0; c < 2; ++c) {
+                    float lq = lrow[nt][c];
+                    lq += __shfl_xor_sync(0xffffffffu, lq, 4);
+                    lq += __shfl_xor_sync(0xffffffffu, lq, 8);
+                    lq += __shfl_xor_sync(0xffffffffu, lq, 16);
+                    const int r = 8 * nt + 2 * t4 + c;
+                    if (r < p.group) {
+                        if (g == 0) {
+                            sm.merge_m[w][r] = mrow[nt][c];
+                            sm.merge_l[w][r] = lq;
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < 8; ++mt) {
+                            merge_o[w][r][16 * mt + g] = o[nt][mt][c];
+                            merge_o[w][r][16 * mt + g + 8] = o[nt][mt][c + 2];
+                        }
+                    }
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
@@ -582,12 +585,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 for (int ww = 0; ww < kDecConsumerWarps; ++ww) {
                     const float wgt = fast_exp2(sm.merge_m[ww][r] - Mu);
                     L += wgt * sm.merge_l[ww][r];
-                    acc += wgt * sm.merge_o[ww][r][d];
+                    acc += wgt * merge_o[ww][r][d];
                 }
                 if (whole) {
                     // each thread reads only its own dim d of merge_o: the
                     // finished row can replace warp 0's partial in place
-                    sm.merge_o[0][r][d] = acc / L;
+                    merge_o[0][r][d] = acc / L;
                 } else {
                     p.ws_o[((int64_t)slot * p.group + r) * 128 + d] = acc;
                     if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
@@ -595,10 +598,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             if (whole) {
                 asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
-                store_rows(p, cur.s, cur.h * p.group, &sm.merge_o[0][0][0], 128, p.group, d,
+                store_rows(p, cur.s, cur.h * p.group, &merge_o[0][0][0], 128, p.group, d,
                            kDecConsumerWarps * 32);
             }
+            fence_proxy_async_smem();  // the producer's next copy into this stage comes after
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+            if (lane == 0) mbar_arrive(&sm.empty[st]);
         }
         cursor_next(cur, p);
     }
@@ -857,22 +862,34 @@ static void bind_workspace(DecodeParams& p, void* ws, int n_ctas)
 
 
 
-template <int ROWS>
+static bool wide_shape(int group, int n_seg) { return group <= 8 && n_seg >= kWideMinSegments; }
+
+// CTAs of a decode launch (the split-K workspace is sized by it).
+static int decode_grid(int group, int n_seg)
+{
+    const int per_sm = wide_shape(group, n_seg) ? 2 : 1;
+    return std::min(per_sm * num_sms(), kMaxPieces - 2);
+}
+
+template <int ROWS, int STAGES, int CTAS_PER_SM>
 static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas,
                          cudaStream_t stream)
 {
-    const size_t smem = sizeof(DecodeSmem<ROWS>) + 1024;
+    auto kernel = decode_attention_kernel<ROWS, STAGES, CTAS_PER_SM>;
+    const size_t smem = sizeof(DecodeSmem<ROWS, STAGES>) + 1024;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr_set[dev]) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(decode_attention_kernel<ROWS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared));
         attr_set[dev] = true;
     }
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
-    cudaError_t e = launch_kernel(decode_attention_kernel<ROWS>, dim3(n_ctas), dim3(kDecThreads),
-                                  smem, stream, ov, c->tm_k, c->tm_v, p);
+    cudaError_t e = launch_kernel(kernel, dim3(n_ctas), dim3(kDecThreads), smem, stream, ov,
+                                  c->tm_k, c->tm_v, p);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention_kernel launch");
     if (int rc = check_launch("decode_attention_kernel")) return rc;
     const int n_items = p.n_seqs * p.view.hkv * p.group;
@@ -889,8 +906,8 @@ extern "C" size_t hx_decode_workspace_bytes(const hx_kv_cache* c, int n_seqs, in
 {
     if (!c || n_seqs < 1 || num_q_heads < 1) return 0;
     const int hkv = c->cfg.num_kv_heads;
-    const int group = num_q_heads / hkv;
-    return decode_ws_bytes(n_seqs, hkv, group < 1 ? 1 : group, std::min(num_sms(), kMaxPieces - 2));
+    const int group = num_q_heads / hkv < 1 ? 1 : num_q_heads / hkv;
+    return decode_ws_bytes(n_seqs, hkv, group, decode_grid(group, n_seqs * hkv));
 }
 
 namespace hx {
@@ -946,16 +963,19 @@ static int run_decode(const hx_kv_cache* c, DecodeParams& p, void* scratch, cuda
         decode_generic_kernel<<<p.n_seqs * p.hq, 128, 0, s>>>(p);
         return check_launch("decode_generic_kernel");
     }
-    const int n_ctas = std::min(num_sms(), kMaxPieces - 2);
+    const int n_seg = p.n_seqs * p.view.hkv;
+    const int n_ctas = decode_grid(p.group, n_seg);
     bind_workspace(p, scratch, n_ctas);
-    if (p.group <= 8) return launch_decode<8>(c, p, n_ctas, s);
-    return launch_decode<16>(c, p, n_ctas, s);
+    if (wide_shape(p.group, n_seg)) return launch_decode<8, 3, 2>(c, p, n_ctas, s);
+    if (p.group <= 8) return launch_decode<8, 6, 1>(c, p, n_ctas, s);
+    return launch_decode<16, 6, 1>(c, p, n_ctas, s);
 }
 
 static size_t needed_scratch(const hx_kv_cache* c, const DecodeParams& p)
 {
     if (!fast_path(c, p)) return 0;
-    return decode_ws_bytes(p.n_seqs, p.view.hkv, p.group, std::min(num_sms(), kMaxPieces - 2));
+    return decode_ws_bytes(p.n_seqs, p.view.hkv, p.group,
+                           decode_grid(p.group, p.n_seqs * p.view.hkv));
 }
 
 }  // namespace hx

@@ -133,6 +133,15 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, ui
                  : "r"(addr));
 }
 
+// Transposes an 8x8 matrix of 16-bit values held one 32-bit pair per lane
+// (lane 4r + c holds row r, columns 2c and 2c+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x)
+{
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 // D = A(16x16 fp16, row) * B(16x8 fp16, col) + D (fp32)
 __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1)
 {
