@@ -162,7 +162,8 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
     const int T = (int)total;
     const int want = (T + kMinTilesPerCta - 1) / kMinTilesPerCta;
     const int n_eff = max(1, min(grid, want));
-    for (int c = lane; c <= n_eff; c += 32) sm.cstart[c] = (int)((long long)T * c / n_eff);
+    // T < 2^31 / kMaxPieces, so T * c fits in 32 bits
+    for (int c = lane; c <= n_eff; c += 32) sm.cstart[c] = (int)((unsigned)T * (unsigned)c / (unsigned)n_eff);
     __syncwarp();
     Sched sc{};
     sc.total = T;
@@ -177,7 +178,9 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
         int run = 0;  // tiles before the current chunk
         for (int base = 0; base < p.n_seqs; base += 32) {
             const int s = base + lane;
-            const int t = s < p.n_seqs ? tiles_of(clamp_len(p.lengths[s], p.view.capacity)) * hkv : 0;
+            const int len = s < p.n_seqs ? clamp_len(p.lengths[s], p.view.capacity) : 0;
+            const int sid = s < p.n_seqs ? p.seq_ids[s] : 0;  // issued with the length load
+            const int t = tiles_of(len) * hkv;
             int incl = t;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -188,15 +191,13 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
             if (hit) {
                 const int src = __ffs(hit) - 1;
                 const int before = run + __shfl_sync(0xffffffffu, incl - t, src);
-                Cursor c{};
-                cursor_load(c, p, base + src);
                 const int off = g0 - before;
-                sc.s = c.s;
-                sc.len = c.len;
-                sc.tiles = c.tiles;
-                sc.seq = c.seq;
-                sc.h = off / c.tiles;
-                sc.j = off % c.tiles;
+                sc.s = base + src;
+                sc.len = __shfl_sync(0xffffffffu, len, src);
+                sc.tiles = tiles_of(sc.len);
+                sc.seq = __shfl_sync(0xffffffffu, sid, src);
+                sc.h = off / sc.tiles;
+                sc.j = off % sc.tiles;
                 break;
             }
             run += __shfl_sync(0xffffffffu, incl, 31);
@@ -575,25 +576,28 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
             const bool whole = c_first == c_last;
             const int seg = cur.s * p.view.hkv + cur.h;
             const int slot = piece_from_seg_start ? seg : (n_seg + cta);
-            for (int r = 0; r < p.group; ++r) {
+            // warp w merges rows w, w+4, ...; each lane four dims (16-byte accesses)
+            for (int r = w; r < p.group; r += kDecConsumerWarps) {
                 float M = -INFINITY;
 #pragma unroll
                 for (int ww = 0; ww < kDecConsumerWarps; ++ww) M = fmaxf(M, sm.merge_m[ww][r]);
                 const float Mu = M == -INFINITY ? 0.f : M;
-                float L = 0.f, acc = 0.f;
+                float L = 0.f;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int ww = 0; ww < kDecConsumerWarps; ++ww) {
                     const float wgt = fast_exp2(sm.merge_m[ww][r] - Mu);
                     L += wgt * sm.merge_l[ww][r];
-                    acc += wgt * merge_o[ww][r][d];
+                    const float4 v = *reinterpret_cast<const float4*>(&merge_o[ww][r][4 * lane]);
+                    acc.x += wgt * v.x; acc.y += wgt * v.y; acc.z += wgt * v.z; acc.w += wgt * v.w;
                 }
                 if (whole) {
-                    // each thread reads only its own dim d of merge_o: the
-                    // finished row can replace warp 0's partial in place
-                    merge_o[0][r][d] = acc / L;
+                    // row r is read and rewritten only by this warp's lanes
+                    *reinterpret_cast<float4*>(&merge_o[0][r][4 * lane]) =
+                        make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
                 } else {
-                    p.ws_o[((int64_t)slot * p.group + r) * 128 + d] = acc;
-                    if (d == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
+                    *reinterpret_cast<float4*>(p.ws_o + ((int64_t)slot * p.group + r) * 128 + 4 * lane) = acc;
+                    if (lane == 0) p.ws_ml[(int64_t)slot * p.group + r] = make_float2(M, L);
                 }
             }
             if (whole) {
@@ -665,7 +669,7 @@ __global__ void __launch_bounds__(128)
     }
     __syncthreads();
     const int a = sh_range[0], b = sh_range[1], T = sh_range[2], n_eff = sh_range[3];
-    auto cstart = [&](int c) { return (int)((long long)T * c / n_eff); };
+    auto cstart = [&](int c) { return (int)((unsigned)T * (unsigned)c / (unsigned)n_eff); };
     if (t == 0) sh_np = 0;
     if (t == 0 && a < b && T > 0) {
         int c = (int)((long long)a * n_eff / T);
