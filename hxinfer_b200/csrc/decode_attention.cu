@@ -392,6 +392,7 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
     float o[NT][8][4];      // O^T: dims 16mt+g (+8) x rows 8nt+2t4 (+1)
     float mrow[NT][2], lrow[NT][2];  // rows 8nt+2t4+c: running max, this lane's partial sum
     bool piece_from_seg_start = false;
+    bool piece_whole = false;  // the piece is its whole segment (no other CTA shares it)
     bool dead = false;  // a bounded wait ran out
     const uint32_t stage_base = smem_u32(&sm.stage[0][0][0]);
     // ldmatrix row addresses (before swizzle) for this lane
@@ -401,6 +402,11 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
         if (i == 0 || cur.j == 0) {
             // new piece: load the packed GQA group of q rows for (s, h)
             piece_from_seg_start = (cur.j == 0);
+            {
+                // global tile range [a, b) of this segment: one CTA or several?
+                const int a = g_first + i - cur.j, b = a + cur.tiles;
+                piece_whole = cta_of_tile(sm.cstart, n_eff, a) == cta_of_tile(sm.cstart, n_eff, b - 1);
+            }
             const int64_t qrow0 = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group) * 128;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
@@ -569,11 +575,7 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
             const int d = threadIdx.x;  // 0..127
-            // global tile range [a, b) of this segment and the CTAs that share it
-            const int a = g_first + i - cur.j, b = a + cur.tiles;
-            const int c_first = cta_of_tile(sm.cstart, n_eff, a);
-            const int c_last = cta_of_tile(sm.cstart, n_eff, b - 1);
-            const bool whole = c_first == c_last;
+            const bool whole = piece_whole;
             const int seg = cur.s * p.view.hkv + cur.h;
             const int slot = piece_from_seg_start ? seg : (n_seg + cta);
             // warp w merges rows w, w+4, ...; each lane four dims (16-byte accesses)
@@ -626,6 +628,7 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
 // Items (segment, q row) are numbered seg * group + r; CTA b takes items b,
 // b + gridDim.x, ...; the launch gives one CTA per item, since each item is
 // a short chain of dependent loads and they overlap best as separate CTAs.
+template <int kSub>  // O loads in flight per lane
 __global__ void __launch_bounds__(128)
     decode_combine_kernel(const DecodeParams p, int grid_ctas)
 {
@@ -693,7 +696,6 @@ __global__ void __launch_bounds__(128)
         const int n_w = np > warp ? (np - warp + 3) / 4 : 0;
         float Mw = -INFINITY, Lw = 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        constexpr int kSub = 8;  // O loads in flight per lane
         for (int base = 0; base < n_w; base += 32) {
             const int cnt = min(32, n_w - base);
             const float2 ml = lane < cnt
@@ -897,7 +899,11 @@ static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention_kernel launch");
     if (int rc = check_launch("decode_attention_kernel")) return rc;
     const int n_items = p.n_seqs * p.view.hkv * p.group;
-    e = launch_kernel(decode_combine_kernel, dim3(n_items), dim3(128), 0, stream, true, p, n_ctas);
+    // Narrow calls (few segments, many pieces each) take 12 O loads per lane
+    // in one round; wide calls have 2-3 pieces per item and keep the 8-load
+    // (64-register) variant, which fits beside two decode CTAs per SM.
+    e = launch_kernel(CTAS_PER_SM == 1 ? decode_combine_kernel<12> : decode_combine_kernel<8>,
+                      dim3(n_items), dim3(128), 0, stream, true, p, n_ctas);
     if (e != cudaSuccess) return cuda_fail(e, "decode_combine_kernel launch");
     return check_launch("decode_combine_kernel");
 }
