@@ -11,6 +11,8 @@ Checks on every rank:
     hxinfer_b200.dist.assemble (all ranks' results exchanged on the host);
   * it matches the unsharded decode of the whole cache within the decode
     attention tolerance (max abs 2e-3, max rel 1e-2 of the output scale).
+The cases cover sequence and kv-head sharding, a rank without sequences, fp32
+output and a call with enough segments for the two-CTAs-per-SM decode shape.
 Then rank 0 waits for an epoch that no rank posts: the bounded device wait
 must end with HX_ERR_TIMEOUT in the status word and leave the context usable.
 Prints "RANK <r> OK" at the end.
@@ -41,6 +43,9 @@ CASES = [
     ("sequences", 8, 4, [700, 1, 129, 4096, 64, 2000, 333], torch.float16),
     ("kv_heads", 4, 2, [1500, 65, 3000, 17], torch.float16),
     ("one_sequence", 8, 4, [2500], torch.float32),  # the other ranks hold no sequence
+    # >= 64 (sequence, kv head) segments per rank: the two-CTAs-per-SM decode shape
+    ("many_segments", 16, 4, [int(x) for x in np.random.default_rng(9).integers(1, 1500, 40)],
+     torch.float16),
 ]
 
 
