@@ -14,7 +14,20 @@ CASES = [
     ([0, 5, 0, 70], 3, 5),            # empty sequences
     (list(np.random.default_rng(4).integers(512, 32769, 64)), 8, 148),  # batched LLaMA-3 shape
     ([3] * 10, 1, 148),               # more CTAs than tiles
+    (list(np.random.default_rng(4).integers(512, 32769, 64)), 8, 296),  # two CTAs per SM
+    (list(np.random.default_rng(5).integers(1, 4000, 40)), 2, 296),     # wide grid, short segments
 ]
+
+
+def test_pieces_per_segment_fit_the_device_bound():
+    """The device keeps at most kMaxPieces (300) pieces per segment, and a
+    launch uses at most 298 CTAs (kMaxPieces - 2): every segment's slot list
+    fits for any lengths."""
+    for lengths, hkv in (([32769], 4), ([200000], 1), ([64] * 3, 8)):
+        for ctas in (148, 296, 298):
+            segs, _ = S.segment_ranges(lengths, hkv)
+            for seg, _, _ in segs:
+                assert len(S.combine_slots(lengths, hkv, ctas, seg)) <= 300
 
 
 @pytest.mark.parametrize("lengths,hkv,ctas", CASES)
