@@ -60,6 +60,8 @@ SIGNATURES = {
     "hx_rope_table_destroy": (_I, [_P]),
     "hx_rope_qk": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "hx_rope_append": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _P]),
+    "hx_qkv_rope_append": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I,
+                                _P, _P, _I, _P]),
     "hx_decode_workspace_bytes": (C.c_size_t, [_P, _I, _I]),
     "hx_decode_attention": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P, _I, _P,
                                  C.c_size_t, _P]),

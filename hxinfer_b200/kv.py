@@ -176,6 +176,27 @@ class KVCache:
                                     _dt(q_out) if q_out is not None else HX_FP16,
                                     _stream(stream)), "rope_append")
 
+    def qkv_rope_append(self, layer: int, x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                        wv: torch.Tensor, seq_ids: torch.Tensor, positions: torch.Tensor,
+                        num_q_heads: int, *, table: "RopeTable | None" = None,
+                        bq=None, bk=None, bv=None, proj_dtype=torch.float16,
+                        q_out: torch.Tensor | None = None, stream=None):
+        """QKV projection of x [n][hidden] with the reference's fp16 weight
+        tensors, fused with bias + RoPE + append (hx_qkv_rope_append); returns
+        q_out [n][Hq*head_dim]."""
+        _need_cuda(x, wq, wk, wv, seq_ids, positions, q_out, bq, bk, bv)
+        n, hidden = x.shape
+        if q_out is None:
+            q_out = torch.empty((n, num_q_heads * self.head_dim), dtype=torch.float16,
+                                device=x.device)
+        pdt = HX_FP32 if proj_dtype == torch.float32 else HX_FP16
+        check(load().hx_qkv_rope_append(
+            self.handle, layer, _ptr(x), _dt(x), hidden, _ptr(wq), _ptr(wk), _ptr(wv), pdt,
+            _ptr(bq), _ptr(bk), _ptr(bv), _ptr(seq_ids), _ptr(positions), n, num_q_heads,
+            table.handle if table is not None else None, _ptr(q_out), _dt(q_out),
+            _stream(stream)), "qkv rope append")
+        return q_out
+
     def workspace_bytes(self, n_seqs: int, num_q_heads: int) -> int:
         return int(load().hx_decode_workspace_bytes(self.handle, n_seqs, num_q_heads))
 

@@ -5,6 +5,7 @@
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
+    python -m hxinfer_b200.profile_case qkv --shape qwen --seqs 1 --layers 28 --iters 20
 
 Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
 prints one JSON line with the CUDA-event time per iteration and the
@@ -220,9 +221,71 @@ def c2_case(a):
                       "decode_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9}))
 
 
+def qkv_case(a):
+    """Decode-step QKV projection of one layer for `seqs` tokens: the fused
+    hx_qkv_rope_append against the unfused chain (three cuBLAS GEMMs through
+    torch, then K1), both captured in CUDA graphs over `layers` layers so the
+    weights (layers x (Hq + 2 Hkv) x 128 x hidden x 2 B) stream from HBM."""
+    hq, hkv, theta = SHAPES[a.shape]
+    hidden = {"qwen": 3584, "llama3": 4096, "llama2": 4096}[a.shape]
+    hd, n, layers = 128, a.seqs, a.layers
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    ws = [[(torch.randn((m * hd, hidden), generator=g, device=dev) * 0.02).half()
+           for m in (hq, hkv, hkv)] for _ in range(layers)]
+    bs = [(torch.randn((m * hd,), generator=g, device=dev) * 0.02).half() for m in (hq, hkv, hkv)]
+    x = torch.randn((n, hidden), generator=g, device=dev).half()
+    cache = kv.KVCache(layers, hkv, hd, n, 64)
+    for s in range(n):
+        cache.reserve(s, 64)
+    table = kv.RopeTable(hd, 64, theta)
+    sid = torch.arange(n, dtype=torch.int32, device=dev)
+    pos = torch.full((n,), 10, dtype=torch.int32, device=dev)
+    q_out = torch.empty((n, hq * hd), dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream()
+
+    def fused():
+        for l in range(layers):
+            cache.qkv_rope_append(l, x, ws[l][0], ws[l][1], ws[l][2], sid, pos, hq, table=table,
+                                  bq=bs[0], bk=bs[1], bv=bs[2], q_out=q_out, stream=stream)
+
+    def chain():
+        for l in range(layers):
+            q = x @ ws[l][0].T
+            k = x @ ws[l][1].T
+            v = x @ ws[l][2].T
+            cache.rope_append(l, k, v, sid, pos, q=q, num_q_heads=hq, table=table, bq=bs[0],
+                              bk=bs[1], bv=bs[2], q_out=q_out, stream=stream)
+
+    res = {}
+    with torch.cuda.stream(stream):
+        for name, fn in (("fused", fused), ("cublas_chain", chain)):
+            fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(a.iters):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            res[name] = 1e3 * e0.elapsed_time(e1) / (a.iters * layers)
+    kv.device_status()
+    wbytes = (hq + 2 * hkv) * hd * hidden * 2
+    print(json.dumps({"case": "qkv", "shape": a.shape, "tokens": n, "layers": layers,
+                      "weight_bytes_per_layer": wbytes,
+                      "fused_us_per_layer": res["fused"], "chain_us_per_layer": res["cublas_chain"],
+                      "fused_gbs": wbytes / (res["fused"] * 1e-6) / 1e9,
+                      "chain_gbs": wbytes / (res["cublas_chain"] * 1e-6) / 1e9}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "qkv"])
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
     ap.add_argument("--len", type=int, default=8192)
@@ -235,7 +298,7 @@ def main():
     a = ap.parse_args()
     torch.cuda.set_device(0)
     {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case,
-     "c2": c2_case}[a.case](a)
+     "c2": c2_case, "qkv": qkv_case}[a.case](a)
 
 
 if __name__ == "__main__":

@@ -183,6 +183,25 @@ int hx_rope_append(hx_kv_cache* cache, int layer, const void* q, const void* k, 
 
 /* ------------------------------------------------------------ attention */
 
+/* The QKV projection fused with K1 (a step beyond the reference's K1
+ * boundary: replaces matmul_qkv_cuda's three cublasGemmEx GEMVs,
+ * matmul_cuda.cu:106-189, and the bias adds in front of hx_rope_append).
+ * For each token i: q = Wq x[i], k = Wk x[i], v = Wv x[i] (fp32 accumulate,
+ * rounded to proj_dtype, the dtype the reference's q/k/v tensors have), then
+ * exactly hx_rope_append's bias + RoPE + append on those values.
+ * x: device [n_tokens][hidden] fp16 or fp32 (fp32 is rounded to fp16 first,
+ * as the reference does); wq/wk/wv: device fp16 [Hq*128][hidden],
+ * [Hkv*128][hidden] row-major (the reference's weight tensors); biases in
+ * proj_dtype, may be NULL.  x and the weights 16-byte aligned; hidden a
+ * multiple of 8, at most 8192; head_dim 128.  Reads each weight row once per
+ * group of 8 tokens: meant for decode batches. */
+int hx_qkv_rope_append(hx_kv_cache* cache, int layer, const void* x, int x_dtype, int hidden,
+                       const void* wq, const void* wk, const void* wv, int proj_dtype,
+                       const void* bq, const void* bk, const void* bv, const int32_t* seq_ids,
+                       const int32_t* positions, int n_tokens, int num_q_heads,
+                       const hx_rope_table* table, void* q_out, int q_out_dtype,
+                       hx_stream_t stream);
+
 /* Workspace bytes hx_decode_attention needs for n_seqs sequences (split-K
  * partial results; device memory owned by the caller, no initialisation
  * needed: every value a call reads is written by that call). */
