@@ -123,19 +123,36 @@ void AttentionLayer::forward(std::shared_ptr<Tensor>& input, std::shared_ptr<Ten
     if (pos < 0 || pos >= config_.seq_len)
         throw std::runtime_error("AttentionLayer: pos outside the cache");
     const int head_dim = config_.dim / config_.head;
-    project(wq_, input, curr_q_);
-    project(wk_, input, curr_k_);
-    project(wv_, input, curr_v_);
     const int32_t* r = detail::ramp(pos + 2);
     const hx_rope_table* table = detail::rope_table(config_, config_.rope_theta, head_dim, pos + 1);
     if (!r || !table) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
     const int at = hx_dtype_of(activation_dtype_);
-    int rc = hx_rope_append(kv_, 0, curr_q_->raw_data_ptr(), curr_k_->raw_data_ptr(),
+    const DataType in_t = input->tensor_data_type();
+    const bool fp16_weights = wq_->tensor_data_type() == DataType::kDataTypeFP16 &&
+                              wk_->tensor_data_type() == DataType::kDataTypeFP16 &&
+                              wv_->tensor_data_type() == DataType::kDataTypeFP16;
+    int rc;
+    if (fp16_weights && head_dim == 128 && config_.dim % 8 == 0 && config_.dim <= 8192 &&
+        (in_t == DataType::kDataTypeFP16 || in_t == DataType::kDataTypeFP32)) {
+        // the reference's fp16-weight projection (matmul_qkv_cuda) fused with
+        // bias + RoPE + append in one launch
+        rc = hx_qkv_rope_append(kv_, 0, input->raw_data_ptr(), hx_dtype_of(in_t), config_.dim,
+                                wq_->raw_data_ptr(), wk_->raw_data_ptr(), wv_->raw_data_ptr(), at,
+                                has_bias_ ? bq_->raw_data_ptr() : nullptr,
+                                has_bias_ ? bk_->raw_data_ptr() : nullptr,
+                                has_bias_ ? bv_->raw_data_ptr() : nullptr, r, r + pos, 1,
+                                config_.head, table, q_rot_->raw_data_ptr(), at, nullptr);
+    } else {
+        project(wq_, input, curr_q_);
+        project(wk_, input, curr_k_);
+        project(wv_, input, curr_v_);
+        rc = hx_rope_append(kv_, 0, curr_q_->raw_data_ptr(), curr_k_->raw_data_ptr(),
                             curr_v_->raw_data_ptr(), at,
                             has_bias_ ? bq_->raw_data_ptr() : nullptr,
                             has_bias_ ? bk_->raw_data_ptr() : nullptr,
                             has_bias_ ? bv_->raw_data_ptr() : nullptr, r, r + pos, 1, config_.head,
                             table, q_rot_->raw_data_ptr(), at, nullptr);
+    }
     if (rc == HX_OK) {
         const size_t ws_bytes = hx_decode_workspace_bytes(kv_, 1, config_.head);
         void* ws = detail::workspace(ws_bytes);

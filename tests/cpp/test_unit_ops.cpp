@@ -60,6 +60,16 @@ static std::shared_ptr<Tensor> cuda_f32(const std::vector<float>& data, std::vec
     return t;
 }
 
+static std::shared_ptr<Tensor> cuda_f16(const std::vector<float>& data, std::vector<int> shape)
+{
+    auto t = std::make_shared<Tensor>(cuda_alloc, shape, DataType::kDataTypeFP16);
+    t->tensor_set_device_type(DeviceType::kDeviceCUDA);
+    std::vector<__half> h(data.size());
+    for (size_t i = 0; i < data.size(); i++) h[i] = __float2half_rn(data[i]);
+    cudaMemcpy(t->raw_data_ptr(), h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice);
+    return t;
+}
+
 static std::vector<float> read_f32(const std::shared_ptr<Tensor>& t)
 {
     std::vector<float> h(t->tensor_total_elements());
@@ -209,10 +219,13 @@ static std::vector<float> matvec(const std::vector<float>& w, const std::vector<
 
 // AttentionLayer::forward (fused bias+RoPE+append, decode) vs the oracle, with
 // exact signed-permutation projections so only the attention path is compared.
-static void test_attention_layer(int Hq, int Hkv, bool bias)
+// fp16_weights: the q/k/v/o weights are fp16 tensors (the reference's model
+// weights), which takes the fused projection (hx_qkv_rope_append); the
+// signed-permutation values are exact in fp16, so the comparison is unchanged.
+static void test_attention_layer(int Hq, int Hkv, bool bias, bool fp16_weights = false)
 {
     std::cout << "=== test_attention_layer (" << Hq << "/" << Hkv << " heads, bias " << bias
-              << ") ===" << std::endl;
+              << ", fp16 weights " << fp16_weights << ") ===" << std::endl;
     const int hd = 128, dim = Hq * hd, kv_dim = Hkv * hd, npos = 70;
     std::mt19937_64 g(100 + Hq + Hkv + bias);
     ModelConfig config{};
@@ -227,8 +240,9 @@ static void test_attention_layer(int Hq, int Hkv, bool bias)
     auto wk_full = signed_perm(dim, g), wv_full = signed_perm(dim, g);
     std::vector<float> wk_h(wk_full.begin(), wk_full.begin() + (size_t)kv_dim * dim);
     std::vector<float> wv_h(wv_full.begin(), wv_full.begin() + (size_t)kv_dim * dim);
-    auto wq = cuda_f32(wq_h, {dim, dim}), wk = cuda_f32(wk_h, {kv_dim, dim});
-    auto wv = cuda_f32(wv_h, {kv_dim, dim}), wo = cuda_f32(wo_h, {dim, dim});
+    auto wmake = fp16_weights ? cuda_f16 : cuda_f32;
+    auto wq = wmake(wq_h, {dim, dim}), wk = wmake(wk_h, {kv_dim, dim});
+    auto wv = wmake(wv_h, {kv_dim, dim}), wo = wmake(wo_h, {dim, dim});
     std::vector<float> bq_h(dim, 0.0f), bk_h(kv_dim, 0.0f), bv_h(kv_dim, 0.0f);
     if (bias) {
         bq_h = normal_f16(g, dim, 0.02f);
@@ -371,6 +385,8 @@ int main()
     test_attention_score_gqa();
     test_attention_layer(4, 4, false);
     test_attention_layer(28, 4, true);
+    test_attention_layer(28, 4, true, true);
+    test_attention_layer(8, 8, false, true);
     test_prefix_cache();
     cudaError_t e = cudaDeviceSynchronize();
     int st = hx_device_status(1);
