@@ -91,6 +91,7 @@ struct Sched {
     int g_first;                   // global index of the first tile
     int total;                     // tiles over all segments
     int n_eff;                     // CTAs that received work
+    int odd_lengths;               // some length is < 1 or above the capacity
 };
 
 template <int ROWS, int STAGES>
@@ -146,13 +147,17 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
     const int lane = threadIdx.x & 31;
     const int hkv = p.view.hkv;
     long long total = 0;
+    bool odd = false;
     for (int base = 0; base < p.n_seqs; base += 32) {
         const int s = base + lane;
-        int t = s < p.n_seqs ? tiles_of(clamp_len(p.lengths[s], p.view.capacity)) : 0;
+        const int len = s < p.n_seqs ? p.lengths[s] : 1;
+        odd |= len < 1 || len > p.view.capacity;
+        int t = tiles_of(clamp_len(len, p.view.capacity)) * (s < p.n_seqs);
 #pragma unroll
         for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
         total += t;
     }
+    odd = __any_sync(0xffffffffu, odd);
     total *= hkv;
     if (total >= (1ll << 31) / kMaxPieces) {
         // the int tile arithmetic below would overflow: refuse the work
@@ -168,6 +173,7 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
     Sched sc{};
     sc.total = T;
     sc.n_eff = n_eff;
+    sc.odd_lengths = odd;
     sc.s = p.n_seqs;
     if (cta < n_eff) {
         sc.g_first = sm.cstart[cta];
@@ -323,7 +329,9 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
     __syncthreads();
     const Sched sc = sm.sched;
     const int count = sc.count;
-    if (cta == 0 && warp == 0) {
+    if (cta == 0 && warp == 0 && sc.odd_lengths) {
+        // only when the plan saw an empty or over-capacity sequence, so the
+        // common call adds no load after the wait to CTA 0's critical path
         pdl_wait();
         zero_empty_outputs(p);
     }
