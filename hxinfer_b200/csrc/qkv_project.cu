@@ -14,6 +14,9 @@
 // K1's arithmetic.  Only the order of the fp32 accumulation differs from
 // cuBLAS's.
 //
+// (For 4-8 tokens, qkv_rope_append_mma_kernel below does the dot products on
+// the tensor cores instead.)
+//
 // Grid: (head slot x 4, token group).  A CTA owns 16 NeoX pairs (d, d + 64)
 // of one head, i.e. 32 weight rows, so the rotation needs no exchange between
 // CTAs; 36-48 heads x 4 = 144-192 CTAs cover the SMs.  Eight warps take four
@@ -68,6 +71,68 @@ template <>
 __device__ __forceinline__ void st_out<float>(float* p, float v)
 {
     *p = v;
+}
+
+// Shared tail of the projection kernels: one thread per (NeoX pair, token);
+// res[lr][t] holds the fp32 dot products of local row lr (d, or d + 64 for
+// lr >= 16) for token t0 + t.
+template <int NTOK, typename TP, typename TO>
+__device__ __forceinline__ void qkv_epilogue(const KVView& view, const float (*res)[NTOK], int slot,
+                                             int qtr, int t0, int nt, const TP* bq, const TP* bk,
+                                             const TP* bv, const int32_t* seq_ids,
+                                             const int32_t* positions, int hq,
+                                             const float2* table, int table_max_pos, TO* q_out,
+                                             int* status)
+{
+    const int hkv = view.hkv;
+    const int i = threadIdx.x & 15, tt = threadIdx.x >> 4;
+    if (tt >= nt) return;
+    const int t = t0 + tt;
+    const int d = 16 * qtr + i;
+    const int seq = seq_ids[t], pos = positions[t];
+    if (seq < 0 || seq >= view.max_seqs || pos < 0 || pos >= view.capacity ||
+        (table && pos >= table_max_pos)) {
+        if (i == 0) record_status(status, HX_ERR_CAPACITY);
+        return;
+    }
+    const float2* cs_row = table ? table + (int64_t)pos * 64 : nullptr;
+    if (slot < hq) {
+        const TP* b = bq ? bq + (int64_t)slot * 128 + d : nullptr;
+        float x1 = proj_bias<TP>(res[i][tt], b), x2 = proj_bias<TP>(res[16 + i][tt], b ? b + 64 : nullptr);
+        if (cs_row) {
+            const float2 cs = cs_row[d];
+            const float o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+            const float o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+            x1 = o1;
+            x2 = o2;
+        }
+        if (q_out) {
+            const int64_t base = ((int64_t)t * hq + slot) * 128 + d;
+            st_out<TO>(q_out + base, x1);
+            st_out<TO>(q_out + base + 64, x2);
+        }
+        return;
+    }
+    const bool is_k = slot < hq + hkv;
+    const int h = is_k ? slot - hq : slot - hq - hkv;
+    const TP* bias = is_k ? bk : bv;
+    const TP* b = bias ? bias + (int64_t)h * 128 + d : nullptr;
+    float x1 = proj_bias<TP>(res[i][tt], b), x2 = proj_bias<TP>(res[16 + i][tt], b ? b + 64 : nullptr);
+    if (is_k && cs_row) {
+        const float2 cs = cs_row[d];
+        const float o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        const float o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+        x1 = o1;
+        x2 = o2;
+    }
+    const int64_t off = token_offset(view, seq, h, pos);
+    if (off < 0) {
+        record_status(status, HX_ERR_CAPACITY);
+        return;
+    }
+    __half* dst = reinterpret_cast<__half*>((is_k ? view.k : view.v) + off);
+    dst[d] = __float2half_rn(x1);
+    dst[d + 64] = __float2half_rn(x2);
 }
 
 template <int NTOK, typename TP, typename TO>
@@ -155,55 +220,97 @@ __global__ void __launch_bounds__(kQkvThreads)
         }
     __syncthreads();
 
-    // epilogue: one thread per (pair, token)
-    const int i = threadIdx.x & 15, tt = threadIdx.x >> 4;
-    if (tt >= nt) return;
-    const int t = t0 + tt;
-    const int d = 16 * qtr + i;
-    const int seq = seq_ids[t], pos = positions[t];
-    if (seq < 0 || seq >= view.max_seqs || pos < 0 || pos >= view.capacity ||
-        (table && pos >= table_max_pos)) {
-        if (i == 0) record_status(status, HX_ERR_CAPACITY);
-        return;
-    }
-    const float2* cs_row = table ? table + (int64_t)pos * 64 : nullptr;
-    if (slot < hq) {
-        const TP* b = bq ? bq + (int64_t)slot * 128 + d : nullptr;
-        float x1 = proj_bias<TP>(res[i][tt], b), x2 = proj_bias<TP>(res[16 + i][tt], b ? b + 64 : nullptr);
-        if (cs_row) {
-            const float2 cs = cs_row[d];
-            const float o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-            const float o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-            x1 = o1;
-            x2 = o2;
+    qkv_epilogue<NTOK, TP, TO>(view, res, slot, qtr, t0, nt, bq, bk, bv, seq_ids, positions, hq,
+                               table, table_max_pos, q_out, status);
+}
+
+// Tensor-core variant for 3-8 tokens (the CUDA-core kernel binds on FMAs
+// there): mma.sync m16n8k16 with the tokens as the M side (rows >= 8 zero)
+// and eight weight rows as the N side.  Warp (row group rg, half kh) takes
+// rows 8rg..8rg+7 and half of `hidden`.  The k index is permuted inside each
+// 32-wide window so that a lane's single 16-byte load of its weight row (and
+// of its token's activations) feeds both k-steps of the window without
+// shuffles: logical k 2t+e (+8) of step s is physical 8t + 4s + e (+2), the
+// same mapping for both operands, so the dot products are unchanged.
+template <int NTOK, typename TP, typename TO>
+__global__ void __launch_bounds__(kQkvThreads)
+    qkv_rope_append_mma_kernel(KVView view, const void* __restrict__ x, int x_f32, int hidden,
+                               int n_tokens, const __half* __restrict__ wq,
+                               const __half* __restrict__ wk, const __half* __restrict__ wv,
+                               const TP* __restrict__ bq, const TP* __restrict__ bk,
+                               const TP* __restrict__ bv, const int32_t* __restrict__ seq_ids,
+                               const int32_t* __restrict__ positions, int hq,
+                               const float2* __restrict__ table, int table_max_pos,
+                               TO* __restrict__ q_out, int* status)
+{
+    static_assert(NTOK <= 8, "tokens are the M side of one m16 tile");
+    extern __shared__ uint4 smem_x[];  // [8][hidden / 8] fp16 chunks, rows >= nt zero
+    __shared__ float part[2][kQkvRows][NTOK];
+    __shared__ float res[kQkvRows][NTOK];
+    pdl_trigger();
+    const int slot = blockIdx.x / 4, qtr = blockIdx.x % 4;
+    const int t0 = blockIdx.y * NTOK;
+    const int nt = min(NTOK, n_tokens - t0);
+    const int hkv = view.hkv;
+    const int chunks = hidden / 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int rg = warp & 3, kh = warp >> 2;
+
+    const __half* wslot = slot < hq ? wq + (int64_t)slot * 128 * hidden
+                        : slot < hq + hkv ? wk + (int64_t)(slot - hq) * 128 * hidden
+                                          : wv + (int64_t)(slot - hq - hkv) * 128 * hidden;
+    const int lr = 8 * rg + g;  // this lane's weight row
+    const int d = 16 * qtr + (lr & 15) + (lr >= 16 ? 64 : 0);
+    const uint4* wrow = reinterpret_cast<const uint4*>(wslot + (int64_t)d * hidden);
+    const int windows = hidden / 32;
+    const int w0 = kh * windows / 2, w1 = (kh + 1) * windows / 2;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(wrow + 4 * w0 + t4));
+
+    pdl_wait();  // x, seq_ids and positions come from the previous kernel
+    for (int e = threadIdx.x; e < 8 * chunks; e += kQkvThreads) {
+        const int t = e / chunks, c = e - t * chunks;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < nt) {
+            const int64_t src = (int64_t)(t0 + t) * hidden + 8 * c;
+            if (x_f32) {
+                const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
+                const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + 4);
+                v = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                               pack_half2(b.z, b.w));
+            } else {
+                v = *reinterpret_cast<const uint4*>(static_cast<const __half*>(x) + src);
+            }
         }
-        if (q_out) {
-            const int64_t base = ((int64_t)t * hq + slot) * 128 + d;
-            st_out<TO>(q_out + base, x1);
-            st_out<TO>(q_out + base + 64, x2);
-        }
-        return;
+        smem_x[t * chunks + c] = v;
     }
-    const bool is_k = slot < hq + hkv;
-    const int h = is_k ? slot - hq : slot - hq - hkv;
-    const TP* bias = is_k ? bk : bv;
-    const TP* b = bias ? bias + (int64_t)h * 128 + d : nullptr;
-    float x1 = proj_bias<TP>(res[i][tt], b), x2 = proj_bias<TP>(res[16 + i][tt], b ? b + 64 : nullptr);
-    if (is_k && cs_row) {
-        const float2 cs = cs_row[d];
-        const float o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-        const float o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-        x1 = o1;
-        x2 = o2;
+    __syncthreads();
+
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint4* xrow = smem_x + g * chunks;  // this lane's token (M row g)
+#pragma unroll 8
+    for (int wdw = w0; wdw < w1; ++wdw) {
+        const uint4 w = __ldcs(wrow + 4 * wdw + t4);  // read once
+        const uint4 xv = xrow[4 * wdw + t4];
+        // step 0: physical 8t4 + {0,1} and + {2,3}; step 1: + {4,5} and + {6,7}
+        const uint32_t a0[4] = {xv.x, 0u, xv.y, 0u};
+        const uint32_t a1[4] = {xv.z, 0u, xv.w, 0u};
+        mma_16816(acc0, a0, w.x, w.y);
+        mma_16816(acc1, a1, w.z, w.w);
     }
-    const int64_t off = token_offset(view, seq, h, pos);
-    if (off < 0) {
-        record_status(status, HX_ERR_CAPACITY);
-        return;
+    // acc[0..1]: token g, rows 8rg + 2t4 (+1); acc[2..3]: tokens g + 8 (none)
+    if (g < NTOK) {
+        part[kh][8 * rg + 2 * t4][g] = acc0[0] + acc1[0];
+        part[kh][8 * rg + 2 * t4 + 1][g] = acc0[1] + acc1[1];
     }
-    __half* dst = reinterpret_cast<__half*>((is_k ? view.k : view.v) + off);
-    dst[d] = __float2half_rn(x1);
-    dst[d + 64] = __float2half_rn(x2);
+    __syncthreads();
+    for (int e = threadIdx.x; e < kQkvRows * NTOK; e += kQkvThreads) {
+        const int row = e / NTOK, t = e % NTOK;
+        res[row][t] = part[0][row][t] + part[1][row][t];
+    }
+    __syncthreads();
+    qkv_epilogue<NTOK, TP, TO>(view, res, slot, qtr, t0, nt, bq, bk, bv, seq_ids, positions, hq,
+                               table, table_max_pos, q_out, status);
 }
 
 template <int NTOK, typename TP, typename TO>
@@ -213,15 +320,17 @@ static int launch_qkv(const hx_kv_cache* c, const KVView& view, const void* x, i
                       const int32_t* positions, int hq, const hx_rope_table* table, void* q_out,
                       cudaStream_t stream)
 {
-    auto kernel = qkv_rope_append_kernel<NTOK, TP, TO>;
-    const size_t smem = (size_t)NTOK * hidden * 2;
-    static bool attr_set[64] = {false};
+    // 4-8 tokens: the tensor-core kernel (whole 32-wide k windows needed)
+    const bool mma = NTOK >= 4 && hidden % 32 == 0;
+    auto kernel = mma ? qkv_rope_append_mma_kernel<NTOK, TP, TO> : qkv_rope_append_kernel<NTOK, TP, TO>;
+    const size_t smem = (size_t)(mma ? 8 : NTOK) * hidden * 2;
+    static bool attr_set[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
+    if (dev < 64 && !attr_set[dev][mma]) {
         HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         NTOK * 8192 * 2));
-        attr_set[dev] = true;
+                                         (mma ? 8 : NTOK) * 8192 * 2));
+        attr_set[dev][mma] = true;
     }
     const dim3 grid((hq + 2 * view.hkv) * 4, (n + NTOK - 1) / NTOK);
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;

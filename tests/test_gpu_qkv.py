@@ -45,6 +45,8 @@ def compare(got, want, what):
     (4096, 32, 8, 8, torch.float16, torch.float16, False),   # LLaMA-3-8B, a full token group
     (4096, 32, 8, 11, torch.float16, torch.float32, True),   # two token groups, fp32 projections
     (1024, 8, 8, 2, torch.float16, torch.float16, True),     # MHA
+    (3584, 28, 4, 5, torch.float16, torch.float16, True),    # tensor-core kernel, 5 of 8 tokens
+    (1000, 8, 4, 6, torch.float16, torch.float16, True),     # hidden not a multiple of 32: CUDA cores
 ])
 def test_fused_projection_matches_the_unfused_chain(hx, hidden, hq, hkv, n, x_dtype, proj_dtype,
                                                     with_bias):
