@@ -200,7 +200,7 @@ def test_decode_fp32_in_out(hx, oracle):
 
 
 def test_decode_qwen_32k(hx, oracle):
-    """The north-star shape: Qwen2.5-7B GQA 28/4, 32,769 positions."""
+    """Single-layer decode at 32k context: Qwen2.5-7B GQA 28/4, 32,769 positions."""
     run_decode(hx, oracle, 28, 4, [32769], seed=32)
 
 
