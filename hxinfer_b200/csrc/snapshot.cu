@@ -96,7 +96,10 @@ static int launch_copy(const hx_kv_cache* c, int seq, int prefix_len, void* buf,
     if (hd_bytes % 16 == 0) {
         const int nblk = (prefix_len + kBlockTokens - 1) / kBlockTokens;
         const int64_t items = (int64_t)c->cfg.num_layers * 2 * c->cfg.num_kv_heads * nblk;
-        const int blocks = (int)std::min<int64_t>(items, (int64_t)num_sms() * 16);
+        // one CTA per run (grid-stride only past 2^20 runs): a fixed grid of
+        // 16 CTAs per SM left a partial last round of runs (7168 runs over 2368
+        // CTAs for a 28-layer, 2048-position snapshot)
+        const int blocks = (int)std::min<int64_t>(items, int64_t(1) << 20);
         snapshot_block_kernel<TO_SNAPSHOT><<<blocks, 256, 0, stream>>>(
             v, c->layer_stride, c->cfg.num_layers, seq, prefix_len, (uint4*)buf, status_word());
         return check_launch("snapshot_block_kernel");
