@@ -82,7 +82,7 @@ struct DecodeParams {
     int* status;
 };
 
-constexpr int kMinTilesPerCta = 4;  // small problems use fewer CTAs, hence fewer pieces
+constexpr int kMinTilesPerCta = 2;  // small problems use fewer CTAs, hence fewer pieces
 
 // The CTA's slice of the flat tile list, computed once by the producer warp.
 struct Sched {

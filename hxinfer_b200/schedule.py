@@ -2,7 +2,7 @@
 
 The decode kernel (csrc/decode_attention.cu) flattens every (sequence,
 kv head) segment into 64-position tiles, ordered sequence-major then kv head
-then tile, and gives CTA c of C = min(grid, ceil(T/4)) the tiles
+then tile, and gives CTA c of C = min(grid, ceil(T/2)) the tiles
 [c*T/C, (c+1)*T/C).  The part of a
 segment inside one CTA is a *piece*.  A piece that starts at its segment's
 first tile stores its partial result in slot ``seq*hkv + head``; a CTA's
@@ -17,7 +17,7 @@ combine step finds every piece, for any lengths and CTA count.
 from __future__ import annotations
 
 BLOCK = 64
-MIN_TILES_PER_CTA = 4  # the device gives each working CTA at least this many tiles
+MIN_TILES_PER_CTA = 2  # the device gives each working CTA at least this many tiles
 
 
 def tiles_of(length: int) -> int:
