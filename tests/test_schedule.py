@@ -57,3 +57,20 @@ def test_combine_finds_exactly_the_pieces(lengths, hkv, ctas):
         assert sorted(S.combine_slots(lengths, hkv, ctas, seg)) == want
         if len(mine) == 1:
             assert mine[0][5]  # the single piece is whole and writes the output
+
+
+def test_schedule_invariants_on_random_batches():
+    """Seeded random batches (lengths 0..70,000, 1-16 kv heads, grids up to
+    298 CTAs): every tile is covered once, piece slots are unique and inside
+    the workspace, and the combine finds exactly the split pieces."""
+    rng = np.random.default_rng(2026)
+    for _ in range(40):
+        n = int(rng.integers(1, 40))
+        lengths = [int(x) for x in rng.integers(0, 70000, n)]
+        if rng.random() < 0.3:
+            lengths[int(rng.integers(0, n))] = 0
+        hkv = int(rng.choice([1, 2, 4, 8, 16]))
+        ctas = int(rng.integers(1, 299))
+        test_every_tile_covered_once(lengths, hkv, ctas)
+        test_slots_unique_and_in_range(lengths, hkv, ctas)
+        test_combine_finds_exactly_the_pieces(lengths, hkv, ctas)
