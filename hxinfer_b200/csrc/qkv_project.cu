@@ -135,8 +135,11 @@ __device__ __forceinline__ void qkv_epilogue(const KVView& view, const float (*r
     dst[d + 64] = __float2half_rn(x2);
 }
 
-template <int NTOK, typename TP, typename TO>
-__global__ void __launch_bounds__(kQkvThreads)
+// BATCH: weight chunks per lane in flight (see the main loop).  BATCH 8 holds
+// ~170 registers, one CTA per SM, for grids that fit the SMs in one wave;
+// BATCH <= 4 fits two CTAs per SM for larger grids.
+template <int NTOK, int BATCH, typename TP, typename TO>
+__global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
     qkv_rope_append_kernel(KVView view, const void* __restrict__ x, int x_f32, int hidden,
                            int n_tokens, const __half* __restrict__ wq,
                            const __half* __restrict__ wk, const __half* __restrict__ wv,
@@ -194,18 +197,32 @@ __global__ void __launch_bounds__(kQkvThreads)
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int t = 0; t < NTOK; ++t) acc[r][t] = 0.f;
-    // more weight loads in flight per lane when there is little arithmetic per chunk
-#pragma unroll(NTOK <= 2 ? 4 : 2)
-    for (int c = lane; c < chunks; c += 32) {
-        uint4 w[4];
+    // The weights are the only HBM traffic and one lane's arithmetic per chunk
+    // is small, so the loop is latency-bound unless many loads are in flight:
+    // each lane issues kBatch chunks x 4 rows (kBatch x 64 B) before it uses
+    // any of them (for 1-2 tokens 128 KB per SM: 8 x 64 B x 256 threads in one
+    // CTA, or 4 x 64 B x 256 threads in each of two).
+    constexpr int kBatch = BATCH;
+    for (int c0 = lane; c0 < chunks; c0 += 32 * kBatch) {
+        uint4 w[kBatch][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) w[r] = __ldcs(wrow[r] + c);  // read once: do not keep in L1/L2
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = c0 + 32 * u;
 #pragma unroll
-        for (int t = 0; t < NTOK; ++t) {
-            if (t < nt) {
-                const uint4 xv = smem_x[t * chunks + c];
+            for (int r = 0; r < 4; ++r)  // read once: do not keep in L1/L2
+                w[u][r] = c < chunks ? __ldcs(wrow[r] + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
 #pragma unroll
-                for (int r = 0; r < 4; ++r) acc[r][t] += dot8(w[r], xv);
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = c0 + 32 * u;
+            if (c >= chunks) break;
+#pragma unroll
+            for (int t = 0; t < NTOK; ++t) {
+                if (t < nt) {
+                    const uint4 xv = smem_x[t * chunks + c];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) acc[r][t] += dot8(w[u][r], xv);
+                }
             }
         }
     }
@@ -322,17 +339,24 @@ static int launch_qkv(const hx_kv_cache* c, const KVView& view, const void* x, i
 {
     // 4-8 tokens: the tensor-core kernel (whole 32-wide k windows needed)
     const bool mma = NTOK >= 4 && hidden % 32 == 0;
-    auto kernel = mma ? qkv_rope_append_mma_kernel<NTOK, TP, TO> : qkv_rope_append_kernel<NTOK, TP, TO>;
+    const dim3 grid((hq + 2 * view.hkv) * 4, (n + NTOK - 1) / NTOK);
+    // 1-2 tokens: 8-chunk batches when the grid is one wave of single CTAs
+    // per SM, else 4-chunk batches at two CTAs per SM (same bytes in flight)
+    const bool one_wave = (int64_t)grid.x * grid.y <= num_sms();
+    const int variant = mma ? 2 : (NTOK <= 2 && one_wave) ? 1 : 0;
+    constexpr int kSmallBatch = NTOK <= 2 ? 4 : 2, kBigBatch = NTOK <= 2 ? 8 : kSmallBatch;
+    auto kernel = variant == 2   ? qkv_rope_append_mma_kernel<NTOK, TP, TO>
+                  : variant == 1 ? qkv_rope_append_kernel<NTOK, kBigBatch, TP, TO>
+                                 : qkv_rope_append_kernel<NTOK, kSmallBatch, TP, TO>;
     const size_t smem = (size_t)(mma ? 8 : NTOK) * hidden * 2;
-    static bool attr_set[64][2] = {};
+    static bool attr_set[64][3] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev][mma]) {
+    if (dev < 64 && !attr_set[dev][variant]) {
         HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (mma ? 8 : NTOK) * 8192 * 2));
-        attr_set[dev][mma] = true;
+        attr_set[dev][variant] = true;
     }
-    const dim3 grid((hq + 2 * view.hkv) * 4, (n + NTOK - 1) / NTOK);
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
     cudaError_t e = launch_kernel(
         kernel, grid, dim3(kQkvThreads), smem, stream, ov, view, x, x_f32, hidden, n,
