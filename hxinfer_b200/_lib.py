@@ -15,7 +15,7 @@ LIB_PATH = os.environ.get("HXINFER_B200_LIB") or os.path.join(PKG, "libhxkv.so")
 
 HX_OK, HX_ERR_INVALID, HX_ERR_CAPACITY, HX_ERR_OOM, HX_ERR_CUDA = 0, 1, 2, 3, 4
 HX_ERR_NCCL, HX_ERR_TIMEOUT, HX_ERR_NOT_FOUND, HX_ERR_UNSUPPORTED = 5, 6, 7, 8
-HX_FP32, HX_FP16 = 1, 3
+HX_FP32, HX_FP16, HX_BF16 = 1, 3, 16
 HX_KV_OVERLAP_LAUNCH = 1
 
 
@@ -72,6 +72,7 @@ SIGNATURES = {
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_kv_restore": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_prefix_hash": (C.c_uint64, [C.POINTER(C.c_int32), C.c_size_t]),
+    "hx_convert": (_I, [_P, _I, _P, _I, C.c_size_t, _P]),
     "hx_dist_handle_bytes": (C.c_size_t, []),
     "hx_dist_create": (_I, [_I, _I, C.c_size_t, C.POINTER(_P)]),
     "hx_dist_export": (_I, [_P, _P]),

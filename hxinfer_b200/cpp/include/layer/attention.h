@@ -2,9 +2,11 @@
 // forward(input, output, pos) and cache getters
 // (hxinfer-engine/include/layer/attention.h:35-102).
 //
-// forward on CUDA tensors: q/k/v projections (cuBLAS GEMV, as the reference),
-// then ONE fused launch for the optional QKV bias + RoPE at `pos` + K/V append
-// (hx_rope_append), then split-K decode attention over pos+1 positions
+// forward on CUDA tensors: with fp16 weights (head_dim 128, dim a multiple of
+// 8 up to 8192) ONE launch does the q/k/v projections + optional bias + RoPE
+// at `pos` + K/V append (hx_qkv_rope_append); otherwise cuBLAS GEMVs (as the
+// reference) followed by one fused bias + RoPE + append launch
+// (hx_rope_append).  Then split-K decode attention over pos+1 positions
 // (hx_decode_attention), then the o projection.  The per-layer cache lives in
 // k_cache_ / v_cache_ ([seq_len, kv_dim] fp16 tensors, head-major inside) and
 // is reached by PrefixCacheManager through get_k_cache()/get_v_cache() and

@@ -13,9 +13,10 @@ import math
 import torch
 
 from . import _lib
-from ._lib import HX_FP16, HX_FP32, check, load
+from ._lib import HX_BF16, HX_FP16, HX_FP32, check, load
 
 _DT = {torch.float16: HX_FP16, torch.float32: HX_FP32}
+_SRC_DT = {torch.float16: HX_FP16, torch.float32: HX_FP32, torch.bfloat16: HX_BF16}
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -46,6 +47,22 @@ def device_status(clear: bool = True) -> int:
     """Device-side status word (synchronises); raises on a recorded error."""
     rc = load().hx_device_status(1 if clear else 0)
     return check(rc, "device status")
+
+
+def convert(dst: torch.Tensor, src: torch.Tensor, stream=None):
+    """Checkpoint dtype conversion on the device (hx_convert): src (fp16,
+    fp32 or bfloat16) into dst (fp16 or fp32), element by element; BF16/FP32
+    -> FP16 rounds to nearest even as the reference's loader does, widening is
+    exact.  dst may share src's memory when the element sizes match (BF16 ->
+    FP16 in place: ``convert(t.view(torch.float16), t)``)."""
+    _need_cuda(dst, src)
+    if src.dtype not in _SRC_DT:
+        raise TypeError(f"unsupported source dtype {src.dtype}")
+    if dst.numel() != src.numel():
+        raise ValueError(f"{dst.numel()} destination elements for {src.numel()} source elements")
+    rc = load().hx_convert(_ptr(dst), _dt(dst), _ptr(src), _SRC_DT[src.dtype], src.numel(),
+                           _stream(stream))
+    check(rc, "hx_convert")
 
 
 def prefix_hash(tokens) -> int:

@@ -57,9 +57,10 @@ enum hx_status {
     HX_ERR_UNSUPPORTED = 8  /* valid request this build does not implement */
 };
 
-/* Element types; the values are the reference's DataType codes
- * (hxinfer-engine/include/base/config.h:5-10). */
-enum hx_dtype { HX_FP32 = 1, HX_FP16 = 3 };
+/* Element types; FP32 and FP16 are the reference's DataType codes
+ * (hxinfer-engine/include/base/config.h:5-10).  BF16 is a checkpoint source
+ * format only (safetensors "BF16"), accepted by hx_convert alone. */
+enum hx_dtype { HX_FP32 = 1, HX_FP16 = 3, HX_BF16 = 16 };
 
 const char* hx_status_string(int status);
 /* Message of the last failed call on this thread ("" if none). */
@@ -326,6 +327,20 @@ int hx_kv_snapshot(const hx_kv_cache* cache, int seq, int prefix_len, void* dst,
  * Replaces PrefixCacheManager::restore's memcpy (prefix_cache.h:135-147). */
 int hx_kv_restore(hx_kv_cache* cache, int seq, int prefix_len, const void* src,
                   size_t src_bytes, hx_stream_t stream);
+
+/* ------------------------------------------------------------ weight loading */
+
+/* Converts n elements of src (device memory, src_dtype) into dst (device
+ * memory, dst_dtype) on `stream`: BF16->FP16, BF16->FP32, FP32->FP16,
+ * FP16->FP32, or a copy when the dtypes are equal.  Narrowing to FP16 rounds
+ * to nearest even, overflowing to infinity, as __float2half does in the
+ * reference's CPU loops; widening is exact.  dst may equal src when both
+ * element sizes are equal (BF16->FP16 in place); otherwise the two ranges
+ * must not overlap.  n = 0 is a no-op.
+ * Replaces the CPU conversion loops of SafetensorsReader::get_tensor_gpu
+ * (model_loaders/src/safetensors_loader.cpp:12-27, 124-197). */
+int hx_convert(void* dst, int dst_dtype, const void* src, int src_dtype, size_t n,
+               hx_stream_t stream);
 
 /* FNV-1a 64 of the token ids (PrefixCacheManager::compute_hash,
  * prefix_cache.h:42-49); host function. */

@@ -8,7 +8,12 @@ Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
   attention.cpp:49-85 with the GQA mapping of attention_score_cuda.cu:20-21,
   softmax_cpu.cpp:6-46, the prefix-cache FNV-1a hash prefix_cache.h:42-49);
 * ``oracle/_ref/libhxref.so`` (optional) — the reference engine's own CPU ops
-  compiled from its sources by ``oracle/Makefile``.
+  compiled from its sources by ``oracle/Makefile``;
+
+and restates in numpy the checkpoint dtype conversions of the reference's
+SafetensorsReader::get_tensor_gpu (model_loaders/src/safetensors_loader.cpp:
+12-27, 124-205), pinned by tests/golden/convert_golden.npz to CUDA's host
+__float2half / __half2float, the functions the reference's loops call.
 
 All inputs are fp32 numpy arrays; fp16 data is rounded with numpy (RNE) and
 upcast before it reaches the oracle, because the reference CPU ops are
@@ -245,3 +250,64 @@ def ref_prefix_roundtrip(layers, dim, head, seq_len, init_kv, overwrite_kv, pref
                                           prb.size, _fp(after_miss), _fp(after_restore), hits)
     assert rc == 0
     return after_miss, after_restore, list(hits)
+
+
+# ---------------------------------------------------------------- checkpoint dtype conversion
+# SafetensorsReader::get_tensor_gpu converts on the CPU before uploading
+# (model_loaders/src/safetensors_loader.cpp:124-205).  numpy's float32 ->
+# float16 cast is the IEEE 754 narrowing (round to nearest even, overflow to
+# infinity) that CUDA's __float2half performs; BF16 -> FP32 is a 16-bit shift.
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    """BF16 bit patterns (uint16) -> fp32, exact: the 16 bits become the top
+    half of the fp32 word (safetensors_loader.cpp:20-24, 135-146)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    """fp32 -> fp16 as __float2half (safetensors_loader.cpp:25, 158-168)."""
+    with np.errstate(over="ignore", invalid="ignore"):
+        return np.asarray(x, dtype=np.float32).astype(np.float16)
+
+
+def convert(raw: np.ndarray, src: str, dst: str) -> np.ndarray:
+    """One tensor as SafetensorsReader::get_tensor_gpu returns it.
+
+    raw: the tensor's bytes (uint8); src: its safetensors dtype ("F32", "F16",
+    "BF16" or "I8"); dst: the target DataType ("FP16", "FP32" or "Int8").
+    Pairs follow safetensors_loader.cpp (BF16->FP16 :125-132, BF16->FP32
+    :135-146, F16->FP16 :149-155, F32->FP16 :158-168, F32->FP32 :171-177,
+    F16->FP32 :180-197) and I8->Int8 (the byte copy of its fallback,
+    :200-205).  Other pairs raise ValueError.
+    """
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    if src == "BF16" and dst == "FP16":
+        return f32_to_f16(bf16_bits_to_f32(raw.view(np.uint16)))
+    if src == "BF16" and dst == "FP32":
+        return bf16_bits_to_f32(raw.view(np.uint16))
+    if src == "F16" and dst == "FP16":
+        return raw.view(np.float16).copy()
+    if src == "F32" and dst == "FP16":
+        return f32_to_f16(raw.view(np.float32))
+    if src == "F32" and dst == "FP32":
+        return raw.view(np.float32).copy()
+    if src == "F16" and dst == "FP32":
+        return raw.view(np.float16).astype(np.float32)
+    if src == "I8" and dst == "Int8":
+        return raw.view(np.int8).copy()
+    raise ValueError(f"no conversion {src} -> {dst}")
+
+
+def canonical_nan_bits(a: np.ndarray) -> np.ndarray:
+    """Bit patterns of a float16 / float32 array with every NaN replaced by
+    one quiet NaN (0x7FFF / 0x7FFFFFFF): NaN outputs are compared as NaN, not
+    by payload."""
+    a = np.asarray(a)
+    if a.dtype == np.float16:
+        bits = a.view(np.uint16).copy()
+        bits[np.isnan(a)] = 0x7FFF
+        return bits
+    assert a.dtype == np.float32
+    bits = a.view(np.uint32).copy()
+    bits[np.isnan(a)] = 0x7FFFFFFF
+    return bits

@@ -79,3 +79,22 @@ def test_gather_endpoint_arguments_are_checked_without_a_device(hxlib):
     assert hxlib.hx_decode_attention_gather(None, 0, None, _lib.HX_FP16, None, None, 0, 1, 1.0,
                                             None, 0, None, 1, 0, _lib.HX_FP16, None, 0,
                                             None) == _lib.HX_ERR_INVALID
+
+
+def test_convert_arguments_are_checked_without_a_device(hxlib):
+    """hx_convert refuses bad dtype pairs, null, overlapping and misaligned
+    pointers before any CUDA call (the addresses below are never touched)."""
+    from hxinfer_b200 import _lib
+    FP16, FP32, BF16, BAD = _lib.HX_FP16, _lib.HX_FP32, _lib.HX_BF16, _lib.HX_ERR_INVALID
+    a, b = 0x10000, 0x80000
+    assert hxlib.hx_convert(None, FP16, None, BF16, 0, None) == _lib.HX_OK  # n = 0: nothing to do
+    assert hxlib.hx_convert(a, BF16, b, FP16, 8, None) == BAD            # BF16 is a source format only
+    assert hxlib.hx_convert(a, FP16, b, 2, 8, None) == BAD               # Int8 is not converted
+    assert hxlib.hx_convert(None, FP16, b, BF16, 8, None) == BAD
+    assert hxlib.hx_convert(a, FP16, None, BF16, 8, None) == BAD
+    assert hxlib.hx_convert(a, FP16, a + 4, FP16, 8, None) == BAD        # overlapping copy
+    assert hxlib.hx_convert(a, FP16, a + 8, FP32, 8, None) == BAD        # overlapping narrowing
+    assert hxlib.hx_convert(a, FP16, a, FP32, 8, None) == BAD            # in place needs equal sizes
+    assert hxlib.hx_convert(a + 1, FP16, b, BF16, 8, None) == BAD        # dst not 2-byte aligned
+    assert hxlib.hx_convert(a + 2, FP32, b, FP16, 8, None) == BAD        # FP32 dst not 4-byte aligned
+    assert b"aligned" in hxlib.hx_last_error()
