@@ -1,7 +1,7 @@
-// dense_model_loader.cpp — config.json and attention weights of a dense
+// attention_loader.cpp — config.json and attention weights of a dense
 // checkpoint (the KV-cache path's part of model_loaders/src/
 // dense_model_loader.cpp:20-156).
-#include "model_loaders/dense_model_loader.h"
+#include "model_loaders/attention_loader.h"
 
 #include <fstream>
 #include <iostream>
@@ -9,6 +9,7 @@
 #include <stdexcept>
 
 #include "json_lite.h"
+#include "model_loaders/safetensors_loader.h"
 
 namespace hxinfer {
 
@@ -51,7 +52,7 @@ std::string string_or(const Value& obj, const char* key, const std::string& fall
 
 }  // namespace
 
-void DenseModelLoader::load_config(const std::string& model_dir, ModelConfig& out_config)
+void AttentionLoader::load_config(const std::string& model_dir, ModelConfig& out_config)
 {
     const std::string config_path = model_dir + "/config.json";
     std::ifstream cf(config_path, std::ios::binary);
@@ -84,14 +85,13 @@ void DenseModelLoader::load_config(const std::string& model_dir, ModelConfig& ou
     }
 }
 
-std::vector<std::shared_ptr<AttentionLayer>> DenseModelLoader::load_attention_layers(
+std::vector<std::shared_ptr<AttentionLayer>> AttentionLoader::load_layers(
     const std::string& model_dir, ModelConfig& out_config,
-    const std::shared_ptr<CUDAAllocator>& cuda_alloc, ModelType type)
+    const std::shared_ptr<CUDAAllocator>& cuda_alloc)
 {
     load_config(model_dir, out_config);
     ModelConfig& c = out_config;
-    std::cout << ">>> [Loader] " << (type == ModelType::Qwen2 ? "Qwen2" : "LLaMA")
-              << " attention: dim=" << c.dim << " layers=" << c.layer << " heads=" << c.head
+    std::cout << ">>> [Loader] attention layers: dim=" << c.dim << " layers=" << c.layer << " heads=" << c.head
               << " kv_heads=" << c.kv_head << " rope_theta=" << c.rope_theta
               << (c.rope_use_yarn ? " (YaRN)" : "") << "\n";
 

@@ -1,15 +1,15 @@
 // test_loader.cpp — drives SafetensorsReader / SafetensorsMultiReader /
-// DenseModelLoader for tests/test_loader.py (CPU subcommands) and
+// AttentionLoader for tests/test_loader.py (CPU subcommands) and
 // tests/test_gpu_weights.py (GPU subcommands).  Prints one result per line;
 // the Python tests hold the expectations.
 //
 //   info <file>                       header as parsed (no CUDA calls)
 //   multi <dir> [probe ...]           directory of shards (no CUDA calls)
-//   config <dir>                      DenseModelLoader::load_config (no CUDA calls)
+//   config <dir>                      AttentionLoader::load_config (no CUDA calls)
 //   fetch <file|dir> <out_dir> <name>:<fp16|fp32|int8> ...
 //                                     get_tensor_gpu, result bytes to <out_dir>/<i>.bin
 //   layers <model_dir> <ref_dir> <npos>
-//                                     load_attention_layers vs. AttentionLayers built from
+//                                     AttentionLoader::load_layers vs. AttentionLayers built from
 //                                     the weights in <ref_dir>; forward outputs compared bitwise
 #include <cuda_runtime.h>
 
@@ -25,7 +25,7 @@
 #include <string>
 #include <vector>
 
-#include "model_loaders/dense_model_loader.h"
+#include "model_loaders/attention_loader.h"
 #include "model_loaders/safetensors_loader.h"
 
 using namespace hxinfer;
@@ -80,7 +80,7 @@ static int cmd_config(const std::string& dir)
 {
     ModelConfig c{};
     try {
-        DenseModelLoader::load_config(dir, c);
+        AttentionLoader::load_config(dir, c);
     } catch (const std::exception& e) {
         std::cout << "error " << e.what() << "\n";
         return 0;
@@ -152,7 +152,7 @@ static int cmd_layers(const std::string& model_dir, const std::string& ref_dir, 
     ModelConfig c{};
     std::vector<std::shared_ptr<AttentionLayer>> loaded;
     try {
-        loaded = DenseModelLoader::load_attention_layers(model_dir, c, alloc, ModelType::Qwen2);
+        loaded = AttentionLoader::load_layers(model_dir, c, alloc);
     } catch (const std::exception& e) {
         std::cout << "error " << e.what() << "\n";
         return 0;

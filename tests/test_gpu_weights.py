@@ -4,7 +4,7 @@ hx_convert (the device-side checkpoint dtype conversion) is checked against
 the oracle's restatement of the reference's CPU loops
 (model_loaders/src/safetensors_loader.cpp:12-27, 124-197), itself pinned to
 CUDA's host __float2half / __half2float by tests/golden/convert_golden.npz.
-SafetensorsReader::get_tensor_gpu and DenseModelLoader::load_attention_layers
+SafetensorsReader::get_tensor_gpu and AttentionLoader::load_layers
 run end to end through tests/cpp/test_loader.  Bar: bit-exact, NaN outputs
 compared as NaN (not by payload).
 """
@@ -188,7 +188,7 @@ def test_multi_reader_takes_the_first_shard(loader_bin, oracle, tmp_path):
     assert np.array_equal(oracle.canonical_nan_bits(got), oracle.canonical_nan_bits(want))
 
 
-# ---------------------------------------------------------------- DenseModelLoader::load_attention_layers
+# ---------------------------------------------------------------- AttentionLoader::load_layers
 
 def bf16_bytes(x: np.ndarray) -> bytes:
     """fp32 -> BF16 bits, round to nearest even (finite inputs)."""

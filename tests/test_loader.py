@@ -1,7 +1,7 @@
 """Checkpoint loading without a GPU: the oracle's dtype conversions pinned to
 the golden vectors of CUDA's host __float2half / __half2float (the functions
 the reference's SafetensorsReader loops call), and the C++ SafetensorsReader /
-SafetensorsMultiReader / DenseModelLoader::load_config on headers, shard
+SafetensorsMultiReader / AttentionLoader::load_config on headers, shard
 directories and config.json files (tests/cpp/test_loader, CPU subcommands
 only).  The reference has no tests for its loader; the cases follow its code
 (model_loaders/src/safetensors_loader.cpp:36-268,
