@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <iostream>
 #include <stdexcept>
@@ -15,9 +16,9 @@ namespace hxinfer {
 
 namespace {
 
-__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int n)
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n)
 {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __float2half_rn(x[i]);
 }
 
@@ -56,6 +57,7 @@ AttentionLayer::AttentionLayer(std::shared_ptr<Allocator> allocator, ModelConfig
 
 void AttentionLayer::init(std::shared_ptr<Allocator> allocator)
 {
+    allocator_ = allocator;
     const int dim = config_.dim;
     if (config_.kv_head <= 0) config_.kv_head = config_.head;
     const int kv_dim = config_.kv_head * (dim / config_.head);
@@ -90,17 +92,32 @@ void AttentionLayer::project(const std::shared_ptr<Tensor>& w, const std::shared
     const int N = static_cast<int>(y->tensor_total_elements());
     if (w->tensor_total_elements() != (size_t)N * K)
         throw std::runtime_error("AttentionLayer: weight shape does not match");
+    project_rows(w, x->raw_data_ptr(), x->tensor_data_type(), y->raw_data_ptr(), y->tensor_data_type(),
+                 1, K, N, x16_);
+}
+
+// rows x K activations times the [n_out][K] weight: one cublasGemmEx,
+// column-major view y^T[n_out][rows] = W[n_out][K] . x^T[K][rows].
+void AttentionLayer::project_rows(const std::shared_ptr<Tensor>& w, const void* x, DataType xt,
+                                  void* y, DataType yt, int rows, int K, int n_out,
+                                  const std::shared_ptr<Tensor>& x16)
+{
+    if (w->tensor_total_elements() != (size_t)n_out * K)
+        throw std::runtime_error("AttentionLayer: weight shape does not match");
     cublasHandle_t h = detail::cublas();
     if (!h) throw std::runtime_error("AttentionLayer: cuBLAS handle");
     const float one = 1.0f, zero = 0.0f;
-    const DataType wt = w->tensor_data_type(), xt = x->tensor_data_type(), yt = y->tensor_data_type();
-    const void* xp = x->raw_data_ptr();
+    const DataType wt = w->tensor_data_type();
+    const void* xp = x;
     cudaDataType_t xct;
     if (wt == DataType::kDataTypeFP16) {
         if (xt == DataType::kDataTypeFP32) {  // weights fp16, activations fp32
-            f32_to_f16_kernel<<<(K + 255) / 256, 256>>>(x->tensor_data_ptr<float>(),
-                                                       x16_->tensor_data_ptr<__half>(), K);
-            xp = x16_->raw_data_ptr();
+            const int64_t n = (int64_t)rows * K;
+            if (x16->tensor_total_elements() < (size_t)n)
+                throw std::runtime_error("AttentionLayer: fp16 staging too small");
+            f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(static_cast<const float*>(x),
+                                                                   x16->tensor_data_ptr<__half>(), n);
+            xp = x16->raw_data_ptr();
         }
         xct = CUDA_R_16F;
     } else if (wt == DataType::kDataTypeFP32 && xt == DataType::kDataTypeFP32) {
@@ -110,18 +127,47 @@ void AttentionLayer::project(const std::shared_ptr<Tensor>& w, const std::shared
     }
     const cudaDataType_t wct = wt == DataType::kDataTypeFP16 ? CUDA_R_16F : CUDA_R_32F;
     const cudaDataType_t yct = yt == DataType::kDataTypeFP16 ? CUDA_R_16F : CUDA_R_32F;
-    cublasStatus_t st = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, N, 1, K, &one, w->raw_data_ptr(),
-                                     wct, K, xp, xct, K, &zero, y->raw_data_ptr(), yct, N,
-                                     CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    cublasStatus_t st = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n_out, rows, K, &one, w->raw_data_ptr(),
+                                     wct, K, xp, xct, K, &zero, y, yct, n_out, CUBLAS_COMPUTE_32F,
+                                     CUBLAS_GEMM_DEFAULT);
     if (st != CUBLAS_STATUS_SUCCESS) throw std::runtime_error("AttentionLayer: cublasGemmEx failed");
+}
+
+void AttentionLayer::reserve_rows(int n)
+{
+    if (n <= rows_cap_) return;
+    int cap = 64;
+    while (cap < n) cap *= 2;
+    cap = std::min(cap, config_.seq_len);
+    const int dim = config_.dim;
+    const int kv_dim = config_.kv_head * (dim / config_.head);
+    q_n_ = make(allocator_, {cap, dim}, activation_dtype_);
+    k_n_ = make(allocator_, {cap, kv_dim}, activation_dtype_);
+    v_n_ = make(allocator_, {cap, kv_dim}, activation_dtype_);
+    q16_n_ = make(allocator_, {cap, dim}, DataType::kDataTypeFP16);
+    attn_n_ = make(allocator_, {cap, dim}, activation_dtype_);
+    x16_n_ = make(allocator_, {cap, std::max(dim, kv_dim)}, DataType::kDataTypeFP16);
+    for (auto* t : {&q_n_, &k_n_, &v_n_, &q16_n_, &attn_n_, &x16_n_})
+        if (!(*t)->raw_data_ptr()) throw std::runtime_error("AttentionLayer: scratch allocation failed");
+    rows_cap_ = cap;
 }
 
 void AttentionLayer::forward(std::shared_ptr<Tensor>& input, std::shared_ptr<Tensor>& output, int pos)
 {
     if (input->tensor_device_type() != DeviceType::kDeviceCUDA || !kv_)
         throw std::runtime_error("AttentionLayer: the B200 build runs on CUDA tensors only");
-    if (pos < 0 || pos >= config_.seq_len)
+    const size_t elems = input->tensor_total_elements();
+    if (config_.dim <= 0 || elems == 0 || elems % (size_t)config_.dim)
+        throw std::runtime_error("AttentionLayer: input is not [n, dim]");
+    if (output->tensor_total_elements() != elems)
+        throw std::runtime_error("AttentionLayer: output must hold as many elements as the input");
+    const size_t n = elems / (size_t)config_.dim;
+    if (pos < 0 || (size_t)pos + n > (size_t)config_.seq_len)
         throw std::runtime_error("AttentionLayer: pos outside the cache");
+    if (n > 1) {
+        forward_tokens(input, output, pos, static_cast<int>(n));
+        return;
+    }
     const int head_dim = config_.dim / config_.head;
     const int32_t* r = detail::ramp(pos + 2);
     const hx_rope_table* table = detail::rope_table(config_, config_.rope_theta, head_dim, pos + 1);
@@ -162,6 +208,65 @@ void AttentionLayer::forward(std::shared_ptr<Tensor>& input, std::shared_ptr<Ten
     }
     if (rc != HX_OK) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
     project(wo_, after_qktv_, output);
+}
+
+// n > 1 tokens of sequence 0 at positions pos .. pos+n-1 (the caller checked
+// pos + n <= seq_len).
+void AttentionLayer::forward_tokens(std::shared_ptr<Tensor>& input, std::shared_ptr<Tensor>& output,
+                                    int pos, int n)
+{
+    const int dim = config_.dim, hq = config_.head, head_dim = dim / hq;
+    const int kv_dim = config_.kv_head * head_dim;
+    const int32_t* r = detail::ramp(pos + n + 1);  // positions r + pos, lengths r + pos + 1
+    const int32_t* seq0 = detail::zeros(n);
+    const hx_rope_table* table = detail::rope_table(config_, config_.rope_theta, head_dim, pos + n);
+    if (!r || !seq0 || !table) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
+    reserve_rows(n);
+    const int at = hx_dtype_of(activation_dtype_);
+    const DataType in_t = input->tensor_data_type();
+    const bool fp16_weights = wq_->tensor_data_type() == DataType::kDataTypeFP16 &&
+                              wk_->tensor_data_type() == DataType::kDataTypeFP16 &&
+                              wv_->tensor_data_type() == DataType::kDataTypeFP16;
+    const void* bq = has_bias_ ? bq_->raw_data_ptr() : nullptr;
+    const void* bk = has_bias_ ? bk_->raw_data_ptr() : nullptr;
+    const void* bv = has_bias_ ? bv_->raw_data_ptr() : nullptr;
+    int rc;
+    if (fp16_weights && head_dim == 128 && dim % 8 == 0 && dim <= 8192 && n <= 8 &&
+        (in_t == DataType::kDataTypeFP16 || in_t == DataType::kDataTypeFP32)) {
+        // up to one token group: the fused projection reads each weight once
+        rc = hx_qkv_rope_append(kv_, 0, input->raw_data_ptr(), hx_dtype_of(in_t), dim,
+                                wq_->raw_data_ptr(), wk_->raw_data_ptr(), wv_->raw_data_ptr(), at, bq, bk,
+                                bv, seq0, r + pos, n, hq, table, q16_n_->raw_data_ptr(), HX_FP16, nullptr);
+    } else {
+        const void* x = input->raw_data_ptr();
+        DataType xt = in_t;
+        if (fp16_weights && in_t == DataType::kDataTypeFP32) {  // one fp16 copy for the three GEMMs
+            const int64_t m = (int64_t)n * dim;
+            f32_to_f16_kernel<<<(unsigned)((m + 255) / 256), 256>>>(input->tensor_data_ptr<float>(),
+                                                                   x16_n_->tensor_data_ptr<__half>(), m);
+            x = x16_n_->raw_data_ptr();
+            xt = DataType::kDataTypeFP16;
+        }
+        project_rows(wq_, x, xt, q_n_->raw_data_ptr(), activation_dtype_, n, dim, dim, x16_n_);
+        project_rows(wk_, x, xt, k_n_->raw_data_ptr(), activation_dtype_, n, dim, kv_dim, x16_n_);
+        project_rows(wv_, x, xt, v_n_->raw_data_ptr(), activation_dtype_, n, dim, kv_dim, x16_n_);
+        rc = hx_rope_append(kv_, 0, q_n_->raw_data_ptr(), k_n_->raw_data_ptr(), v_n_->raw_data_ptr(), at, bq,
+                            bk, bv, seq0, r + pos, n, hq, table, q16_n_->raw_data_ptr(), HX_FP16, nullptr);
+    }
+    const float scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    if (rc == HX_OK && head_dim == 128) {
+        rc = hx_prefill_attention(kv_, 0, q16_n_->raw_data_ptr(), 0, pos, n, hq, scale,
+                                  attn_n_->raw_data_ptr(), at, nullptr);
+    } else if (rc == HX_OK) {
+        // causal attention as n decode rows over the same sequence
+        const size_t ws_bytes = hx_decode_workspace_bytes(kv_, n, hq);
+        void* ws = detail::workspace(ws_bytes);
+        rc = hx_decode_attention(kv_, 0, q16_n_->raw_data_ptr(), HX_FP16, seq0, r + pos + 1, n, hq, scale,
+                                 attn_n_->raw_data_ptr(), at, ws, ws_bytes, nullptr);
+    }
+    if (rc != HX_OK) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
+    project_rows(wo_, attn_n_->raw_data_ptr(), activation_dtype_, output->raw_data_ptr(),
+                 output->tensor_data_type(), n, dim, dim, x16_n_);
 }
 
 }  // namespace hxinfer

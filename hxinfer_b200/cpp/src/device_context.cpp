@@ -17,6 +17,8 @@ namespace {
 struct DeviceState {
     int32_t* ramp = nullptr;
     int ramp_n = 0;
+    int32_t* zeros = nullptr;
+    int zeros_n = 0;
     void* ws = nullptr;
     size_t ws_bytes = 0;
     cublasHandle_t cublas = nullptr;
@@ -54,6 +56,27 @@ const int32_t* ramp(int n)
         s.ramp_n = m;
     }
     return s.ramp;
+}
+
+const int32_t* zeros(int n)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState& s = state();
+    if (n > s.zeros_n) {
+        int m = 256;
+        while (m < n) m *= 2;
+        std::vector<int32_t> h(m, 0);
+        int32_t* d = nullptr;
+        if (cudaMalloc(&d, sizeof(int32_t) * m) != cudaSuccess) return nullptr;
+        if (cudaMemcpy(d, h.data(), sizeof(int32_t) * m, cudaMemcpyHostToDevice) != cudaSuccess) {
+            cudaFree(d);
+            return nullptr;
+        }
+        if (s.zeros) cudaFree(s.zeros);
+        s.zeros = d;
+        s.zeros_n = m;
+    }
+    return s.zeros;
 }
 
 void* workspace(size_t bytes)

@@ -13,6 +13,9 @@ namespace detail {
 
 // Device pointer to int32 values [0, n) (valid until a larger n is asked for).
 const int32_t* ramp(int n);
+// Device pointer to n int32 zeros (sequence ids of a one-sequence batch; valid
+// until a larger n is asked for).
+const int32_t* zeros(int n);
 // Device workspace of at least `bytes` bytes.
 void* workspace(size_t bytes);
 cublasHandle_t cublas();

@@ -1,6 +1,6 @@
 // test_loader.cpp — drives SafetensorsReader / SafetensorsMultiReader /
 // AttentionLoader for tests/test_loader.py (CPU subcommands) and
-// tests/test_gpu_weights.py (GPU subcommands).  Prints one result per line;
+// tests/test_zz_gpu_weights.py (GPU subcommands).  Prints one result per line;
 // the Python tests hold the expectations.
 //
 //   info <file>                       header as parsed (no CUDA calls)

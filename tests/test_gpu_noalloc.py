@@ -5,8 +5,7 @@ scratch array instead of a caller workspace.
 
 Checked through the C ABI against hx_decode_attention (caller workspace) on
 two calls in a row, within the attention tolerance of the other tests
-(2e-3 absolute + 1e-2 relative).  Collected last so that a stop at the first
-failure has already run every other test; it also passes run alone."""
+(2e-3 absolute + 1e-2 relative); it also passes run alone."""
 import ctypes as C
 import math
 

@@ -6,7 +6,8 @@ the oracle's restatement of the reference's CPU loops
 CUDA's host __float2half / __half2float by tests/golden/convert_golden.npz.
 SafetensorsReader::get_tensor_gpu and AttentionLoader::load_layers
 run end to end through tests/cpp/test_loader.  Bar: bit-exact, NaN outputs
-compared as NaN (not by payload).
+compared as NaN (not by payload).  Collected after the other GPU tests, so
+that a stop at the first failure has already run them.
 """
 import json
 import os
