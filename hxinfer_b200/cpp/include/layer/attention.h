@@ -14,7 +14,7 @@
 // projections become GEMMs (the fused launch for n <= 8), one bias + RoPE +
 // append launch covers the n tokens, and causal prefill attention
 // (hx_prefill_attention, tcgen05; head_dim 128) or, for other head sizes, one
-// decode row per token replaces the per-token decode.  Row i equals what the
+// decode call per token replaces the per-token decode.  Row i equals what the
 // i-th of n single-token calls returns, up to fp32 summation order and the
 // rotated q being held in fp16 for the prefill kernel.
 //

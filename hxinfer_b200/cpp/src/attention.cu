@@ -258,11 +258,17 @@ void AttentionLayer::forward_tokens(std::shared_ptr<Tensor>& input, std::shared_
         rc = hx_prefill_attention(kv_, 0, q16_n_->raw_data_ptr(), 0, pos, n, hq, scale,
                                   attn_n_->raw_data_ptr(), at, nullptr);
     } else if (rc == HX_OK) {
-        // causal attention as n decode rows over the same sequence
-        const size_t ws_bytes = hx_decode_workspace_bytes(kv_, n, hq);
+        // no tcgen05 prefill for this head size: one decode call per token
+        // over positions [0, pos + i] (the layer's cache holds one sequence,
+        // so the rows cannot go into one call as separate sequences)
+        const size_t ws_bytes = hx_decode_workspace_bytes(kv_, 1, hq);
         void* ws = detail::workspace(ws_bytes);
-        rc = hx_decode_attention(kv_, 0, q16_n_->raw_data_ptr(), HX_FP16, seq0, r + pos + 1, n, hq, scale,
-                                 attn_n_->raw_data_ptr(), at, ws, ws_bytes, nullptr);
+        const size_t out_row = (size_t)dim * DataTypeSize(activation_dtype_);
+        const char* q16 = static_cast<const char*>(q16_n_->raw_data_ptr());
+        char* attn = static_cast<char*>(attn_n_->raw_data_ptr());
+        for (int i = 0; i < n && rc == HX_OK; ++i)
+            rc = hx_decode_attention(kv_, 0, q16 + (size_t)i * dim * 2, HX_FP16, seq0, r + pos + 1 + i, 1, hq,
+                                     scale, attn + i * out_row, at, ws, ws_bytes, nullptr);
     }
     if (rc != HX_OK) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
     project_rows(wo_, attn_n_->raw_data_ptr(), activation_dtype_, output->raw_data_ptr(),

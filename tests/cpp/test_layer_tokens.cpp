@@ -9,7 +9,7 @@
 // must equal the oracle's fp16 rows bit for bit; outputs are compared within
 // the attention tolerance (2e-3 + 1e-2 |ref|).  Calls mix chunk sizes so that
 // each path runs: n <= 8 with fp16 weights (fused projection), larger n
-// (cuBLAS GEMMs), head_dim 128 (tcgen05 prefill) and 64 (one decode row per
+// (cuBLAS GEMMs), head_dim 128 (tcgen05 prefill) and 64 (one decode call per
 // token), chunks crossing 64-position blocks, and a cache filled to a
 // capacity that is not a multiple of 64.  Exit status = number of failures.
 #include <cuda_fp16.h>
@@ -166,7 +166,7 @@ int main()
     test_tokens(4, 4, 128, false, false, 512, {2, 61, 1, 200, 9});
     // capacity 1000 (not a multiple of 64) filled to the last position
     test_tokens(4, 2, 128, true, true, 1000, {600, 399, 1});
-    // head_dim 64: no tcgen05 prefill; one decode row per token
+    // head_dim 64: no tcgen05 prefill; one decode call per token
     test_tokens(4, 2, 64, true, true, 512, {1, 6, 70, 3, 150});
     test_shape_errors();
     cudaError_t e = cudaDeviceSynchronize();
