@@ -8,6 +8,8 @@
 //   config <dir>                      AttentionLoader::load_config (no CUDA calls)
 //   fetch <file|dir> <out_dir> <name>:<fp16|fp32|int8> ...
 //                                     get_tensor_gpu, result bytes to <out_dir>/<i>.bin
+//   json <file>                       each line parsed by json_lite: "ok <canonical JSON>"
+//                                     or "error" (no CUDA calls)
 //   layers <model_dir> <ref_dir> <npos>
 //                                     AttentionLoader::load_layers vs. AttentionLayers built from
 //                                     the weights in <ref_dir>; forward outputs compared bitwise
@@ -25,6 +27,7 @@
 #include <string>
 #include <vector>
 
+#include "json_lite.h"
 #include "model_loaders/attention_loader.h"
 #include "model_loaders/safetensors_loader.h"
 
@@ -73,6 +76,81 @@ static int cmd_multi(const std::string& dir, int argc, char** argv)
     std::cout << "n " << m.num_tensors() << "\n";
     for (const auto& name : m.tensor_names()) std::cout << "m " << name << "\n";
     for (int i = 0; i < argc; ++i) std::cout << "has " << argv[i] << " " << (m.has_tensor(argv[i]) ? 1 : 0) << "\n";
+    return 0;
+}
+
+// Canonical JSON text of a parsed value: members in document order, numbers
+// as int64 or %.17g, strings with only the escapes JSON requires.
+static void dump(const json_lite::Value& v, std::string& out)
+{
+    using json_lite::Value;
+    switch (v.kind) {
+    case Value::Null: out += "null"; break;
+    case Value::Bool: out += v.boolean ? "true" : "false"; break;
+    case Value::Number: {
+        char buf[40];
+        if (v.is_int)
+            std::snprintf(buf, sizeof buf, "%lld", (long long)v.integer);
+        else
+            std::snprintf(buf, sizeof buf, "%.17g", v.number);
+        out += buf;
+        break;
+    }
+    case Value::String:
+        out += '"';
+        for (unsigned char c : v.str) {
+            if (c == '"' || c == '\\') {
+                out += '\\';
+                out += (char)c;
+            } else if (c < 0x20) {
+                char buf[8];
+                std::snprintf(buf, sizeof buf, "\\u%04x", c);
+                out += buf;
+            } else {
+                out += (char)c;
+            }
+        }
+        out += '"';
+        break;
+    case Value::Array:
+        out += '[';
+        for (size_t i = 0; i < v.items.size(); ++i) {
+            if (i) out += ',';
+            dump(v.items[i], out);
+        }
+        out += ']';
+        break;
+    case Value::Object:
+        out += '{';
+        for (size_t i = 0; i < v.members.size(); ++i) {
+            if (i) out += ',';
+            json_lite::Value key;
+            key.kind = Value::String;
+            key.str = v.members[i].first;
+            dump(key, out);
+            out += ':';
+            dump(v.members[i].second, out);
+        }
+        out += '}';
+        break;
+    }
+}
+
+static int cmd_json(const std::string& path)
+{
+    std::ifstream f(path, std::ios::binary);
+    std::string line;
+    while (std::getline(f, line)) {
+        json_lite::Value v;
+        std::string err;
+        if (json_lite::parse(line.data(), line.data() + line.size(), v, &err)) {
+            std::string out;
+            dump(v, out);
+            std::cout << "ok " << out << "\n";
+        } else {
+            std::cout << "error\n";
+        }
+    }
     return 0;
 }
 
@@ -212,6 +290,7 @@ int main(int argc, char** argv)
     if (cmd == "info") return cmd_info(argv[2]);
     if (cmd == "multi") return cmd_multi(argv[2], argc - 3, argv + 3);
     if (cmd == "config") return cmd_config(argv[2]);
+    if (cmd == "json") return cmd_json(argv[2]);
     if (cmd == "fetch" && argc >= 4) return cmd_fetch(argv[2], argv[3], argc - 4, argv + 4);
     if (cmd == "layers" && argc == 5) return cmd_layers(argv[2], argv[3], std::atoi(argv[4]));
     std::cerr << "bad arguments\n";

@@ -2,8 +2,8 @@
 the golden vectors of CUDA's host __float2half / __half2float (the functions
 the reference's SafetensorsReader loops call), and the C++ SafetensorsReader /
 SafetensorsMultiReader / AttentionLoader::load_config on headers, shard
-directories and config.json files (tests/cpp/test_loader, CPU subcommands
-only).  The reference has no tests for its loader; the cases follow its code
+directories and config.json files, and its JSON reader against Python's
+(tests/cpp/test_loader, CPU subcommands only).  The reference has no tests for its loader; the cases follow its code
 (model_loaders/src/safetensors_loader.cpp:36-268,
 model_loaders/src/dense_model_loader.cpp:27-52) and the safetensors format."""
 import json
@@ -12,6 +12,8 @@ import sys
 
 import numpy as np
 import pytest
+from hypothesis import HealthCheck, given, settings
+from hypothesis import strategies as st
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -237,3 +239,56 @@ def test_load_config_errors(loader_bin, tmp_path):
     assert "hidden_size" in run_loader("config", _config(tmp_path, "nohidden", bad))[0]
     assert run_loader("config", _config(tmp_path, "garbage", "{oops"))[0].startswith("error")
 
+
+
+# ---------------------------------------------------------------- the JSON reader
+
+def _json_lines(loader_bin, tmp_path, docs):
+    p = tmp_path / "docs.jsonl"
+    p.write_bytes(b"\n".join(d.encode() if isinstance(d, str) else d for d in docs) + b"\n")
+    out = run_loader("json", str(p))
+    assert len(out) == len(docs)
+    return out
+
+
+_JSON_SCALARS = (st.none() | st.booleans() | st.integers(-(2**63), 2**63 - 1) |
+                 st.floats(allow_nan=False, allow_infinity=False) |
+                 st.text(alphabet=st.characters(blacklist_categories=("Cs",)), max_size=12))
+_JSON_VALUES = st.recursive(
+    _JSON_SCALARS,
+    lambda inner: st.lists(inner, max_size=5) |
+    st.dictionaries(st.text(alphabet=st.characters(blacklist_categories=("Cs",)), max_size=8), inner,
+                    max_size=5),
+    max_leaves=25)
+
+
+@settings(max_examples=1, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.lists(st.tuples(_JSON_VALUES, st.booleans()), min_size=300, max_size=300))
+def test_json_reader_round_trips_random_documents(loader_bin, tmp_path, docs):
+    """Random documents (escaped or raw UTF-8) read by json_lite and written
+    back canonically load to the same Python values."""
+    texts = [json.dumps(v, ensure_ascii=a) for v, a in docs]
+    out = _json_lines(loader_bin, tmp_path, texts)
+    for (v, _), text, line in zip(docs, texts, out):
+        assert line.startswith("ok "), text
+        assert json.loads(line[3:]) == v, text
+
+
+def test_json_reader_rejects_what_rfc8259_rejects(loader_bin, tmp_path):
+    invalid = ["{", "[1,]", '{"a":}', "01", "1.", ".5", "-", "+1", "tru", "nul", '"\\x"', '"abc',
+               "[1 2]", '{"a" 1}', "{1:2}", "1e", "1e+", "--1", '"\t"', "[]]", "{} {}", "",
+               "NaN", "Infinity", "-Infinity", '"\\ud800"', '"\\udc00x"', '"\\u12"', "[" * 70 + "]" * 70]
+    out = _json_lines(loader_bin, tmp_path, invalid)
+    assert [d for d, line in zip(invalid, out) if line != "error"] == []
+    for d in invalid[:21]:  # Python's reader rejects these too
+        with pytest.raises(ValueError):
+            json.loads(d)
+
+
+def test_json_reader_keeps_int64_exact(loader_bin, tmp_path):
+    docs = ["9223372036854775807", "-9223372036854775808", "[0, -0, 18446744073709551615]",
+            '{"data_offsets": [4294967296, 1099511627776]}']
+    out = _json_lines(loader_bin, tmp_path, docs)
+    assert out[0] == "ok 9223372036854775807" and out[1] == "ok -9223372036854775808"
+    assert out[2] == "ok [0,0,1.8446744073709552e+19]"  # past int64: a double
+    assert out[3] == 'ok {"data_offsets":[4294967296,1099511627776]}'
