@@ -6,6 +6,7 @@
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
     python -m hxinfer_b200.profile_case qkv --shape qwen --seqs 1 --layers 28 --iters 20
+    python -m hxinfer_b200.profile_case convert --mib 1024 --iters 10
 
 Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
 prints one JSON line with the CUDA-event time per iteration and the
@@ -283,9 +284,39 @@ def qkv_case(a):
                       "chain_gbs": wbytes / (res["cublas_chain"] * 1e-6) / 1e9}))
 
 
+def convert_case(a):
+    """Checkpoint dtype conversion on the device (hx_convert): BF16 -> FP16
+    in place (the loader's common case; 2 + 2 bytes per element) and
+    FP32 -> FP16 out of place (4 + 2 bytes per element), --mib MiB of source."""
+    n16 = a.mib * (1 << 20) // 2
+    n32 = a.mib * (1 << 20) // 4
+    g = torch.Generator(device="cuda").manual_seed(1)
+    bf = torch.randn(n16, device="cuda", generator=g).to(torch.bfloat16)
+    f32 = torch.randn(n32, device="cuda", generator=g)
+    h16 = torch.empty(n32, dtype=torch.float16, device="cuda")
+    res = {}
+    for name, run, nbytes in (
+            ("bf16_to_fp16_inplace", lambda: kv.convert(bf.view(torch.float16), bf), 4 * n16),
+            ("fp32_to_fp16", lambda: kv.convert(h16, f32), 6 * n32)):
+        run()  # warm-up
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.iters + 1)]
+        ev[0].record()
+        for i in range(a.iters):
+            run()
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(a.iters)]
+        best = min(ms)
+        res[name] = {"ms_best": best, "ms_mean": sum(ms) / len(ms), "bytes": nbytes,
+                     "gbs_best": nbytes / (best * 1e-3) / 1e9}
+    kv.device_status()
+    print(json.dumps({"case": "convert", "mib": a.mib, **res}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "qkv"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "qkv", "convert"])
+    ap.add_argument("--mib", type=int, default=1024, help="convert: MiB of source data")
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
     ap.add_argument("--len", type=int, default=8192)
@@ -298,7 +329,7 @@ def main():
     a = ap.parse_args()
     torch.cuda.set_device(0)
     {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case,
-     "c2": c2_case, "qkv": qkv_case}[a.case](a)
+     "c2": c2_case, "qkv": qkv_case, "convert": convert_case}[a.case](a)
 
 
 if __name__ == "__main__":
