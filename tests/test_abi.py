@@ -98,3 +98,26 @@ def test_convert_arguments_are_checked_without_a_device(hxlib):
     assert hxlib.hx_convert(a + 1, FP16, b, BF16, 8, None) == BAD        # dst not 2-byte aligned
     assert hxlib.hx_convert(a + 2, FP32, b, FP16, 8, None) == BAD        # FP32 dst not 4-byte aligned
     assert b"aligned" in hxlib.hx_last_error()
+
+
+def test_header_is_c99_and_links_from_c(tmp_path):
+    """The boundary is a C ABI: include/hx_kv.h compiles as strict C99, and a
+    C program that takes the address of every declared function links
+    against libhxkv.so (unmangled names, matching declarations)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if not gcc:
+        import pytest
+        pytest.skip("gcc not present")
+    inc, pkg = os.path.join(ROOT, "include"), os.path.join(ROOT, "hxinfer_b200")
+    names = sorted(declared_functions())
+    src = tmp_path / "uses_every_entry_point.c"
+    src.write_text("#include <stddef.h>\n#include <stdint.h>\n#include \"hx_kv.h\"\n"
+                   "void* const entry_points[] = {\n" +
+                   "".join(f"    (void*){n},\n" for n in names) + "};\n"
+                   "int main(void) { return entry_points[0] == NULL; }\n")
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", f"-I{inc}", str(src),
+                        "-o", str(tmp_path / "a.out"),
+                        f"-L{pkg}", "-lhxkv", f"-Wl,-rpath,{pkg}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
