@@ -193,3 +193,43 @@ def test_hash_matches_reference_fresh(ref):
     for n in (0, 1, 7, 300):
         t = rng.integers(-5, 152064, n).astype(np.int32)
         assert ref.fnv1a64(t) == ref.ref_hash(t)
+
+
+# --------------------------------------------------------------- random inputs against the built reference
+
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+from hypothesis.extra.numpy import arrays  # noqa: E402
+
+_SETTINGS = settings(max_examples=60, deadline=None,
+                     suppress_health_check=[HealthCheck.function_scoped_fixture])
+
+
+@_SETTINGS
+@given(hkv=st.sampled_from([1, 2, 4, 8]), group=st.sampled_from([1, 2, 4, 7]),
+       hd=st.sampled_from([64, 128, 256]), rows=st.integers(1, 3), step=st.integers(0, 131071),
+       theta=st.sampled_from([1e4, 5e5, 1e6]) | st.floats(100.0, 1e7, width=32),
+       seed=st.integers(0, 2**31 - 1), scale=st.sampled_from([1.0, 1e-3, 300.0]))
+def test_rope_matches_reference_on_random_inputs(ref, hkv, group, hd, rows, step, theta, seed, scale):
+    """Bit-exact RoPE for random head layouts, positions, bases and magnitudes."""
+    hq = hkv * group
+    rng = np.random.default_rng(seed)
+    q = ref.f16(rng.standard_normal((rows, hq * hd)) * scale)
+    k = ref.f16(rng.standard_normal((rows, hkv * hd)) * scale)
+    rq, rk = ref.ref_rope(q, k, hq, hkv, hd, step, float(theta))
+    assert np.array_equal(bits(ref.rope(q, hq, hd, step, float(theta))), bits(rq))
+    assert np.array_equal(bits(ref.rope(k, hkv, hd, step, float(theta))), bits(rk))
+
+
+@_SETTINGS
+@given(x=arrays(np.float32, st.integers(1, 5000),
+                elements=st.floats(-80.0, 80.0, width=32, allow_nan=False)))
+def test_softmax_matches_reference_on_random_inputs(ref, x):
+    """Bit-exact safe softmax (max-subtracted exponentials over their sum)."""
+    assert np.array_equal(bits(ref.softmax(x)), bits(ref.ref_softmax(x)))
+
+
+@_SETTINGS
+@given(t=arrays(np.int32, st.integers(0, 2000), elements=st.integers(-2**31, 2**31 - 1)))
+def test_hash_matches_reference_on_random_inputs(ref, t):
+    assert ref.fnv1a64(t) == ref.ref_hash(t)
