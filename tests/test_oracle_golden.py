@@ -233,3 +233,29 @@ def test_softmax_matches_reference_on_random_inputs(ref, x):
 @given(t=arrays(np.int32, st.integers(0, 2000), elements=st.integers(-2**31, 2**31 - 1)))
 def test_hash_matches_reference_on_random_inputs(ref, t):
     assert ref.fnv1a64(t) == ref.ref_hash(t)
+
+
+@settings(max_examples=25, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(head=st.integers(1, 6), hd=st.sampled_from([32, 64, 128]), npos=st.integers(1, 24),
+       theta=st.sampled_from([1e4, 1e6]), seed=st.integers(0, 2**31 - 1))
+def test_attention_layer_matches_reference_on_random_inputs(ref, head, hd, npos, theta, seed):
+    """The reference's CPU AttentionLayer (one token per forward) against the
+    oracle's RoPE + decode attention, bit-exact, with exact signed-permutation
+    projections."""
+    rng = np.random.default_rng(seed)
+    dim = head * hd
+    ws = []
+    for _ in range(4):
+        w = np.zeros((dim, dim), np.float32)
+        w[np.arange(dim), rng.permutation(dim)] = rng.choice([-1.0, 0.5, 1.0, 2.0], dim)
+        ws.append(w)
+    x = ref.f16(rng.standard_normal((npos, dim)))
+    want = ref.ref_attention_layer(dim, head, theta, *ws, x)
+    K = np.zeros((npos, dim), np.float32)
+    V = np.zeros((npos, dim), np.float32)
+    for p in range(npos):
+        q = ref.rope((ws[0] @ x[p])[None].astype(np.float32), head, hd, p, theta)[0]
+        K[p] = ref.rope((ws[1] @ x[p])[None].astype(np.float32), head, hd, p, theta)[0]
+        V[p] = (ws[2] @ x[p]).astype(np.float32)
+        got = (ws[3] @ ref.decode_attention(q, K[:p + 1], V[:p + 1], head, head, hd)).astype(np.float32)
+        assert np.array_equal(bits(got), bits(want[p])), p
