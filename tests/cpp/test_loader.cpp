@@ -10,12 +10,16 @@
 //                                     get_tensor_gpu, result bytes to <out_dir>/<i>.bin
 //   json <file>                       each line parsed by json_lite: "ok <canonical JSON>"
 //                                     or "error" (no CUDA calls)
+//   time <file> <name> <fp16|fp32> <reps>
+//                                     wall time of get_tensor_gpu (file bytes in the page
+//                                     cache after the first call): "time <best ms> <file bytes>"
 //   layers <model_dir> <ref_dir> <npos>
 //                                     AttentionLoader::load_layers vs. AttentionLayers built from
 //                                     the weights in <ref_dir>; forward outputs compared bitwise
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -211,6 +215,31 @@ static int cmd_fetch(const std::string& path, const std::string& out_dir, int ar
     return 0;
 }
 
+static int cmd_time(const std::string& path, const std::string& name, const std::string& want, int reps)
+{
+    auto alloc = std::make_shared<CUDAAllocator>();
+    SafetensorsReader r;
+    if (!r.load(path) || !r.has_tensor(name)) {
+        std::cout << "load fail\n";
+        return 0;
+    }
+    const DataType dt = want == "fp32" ? DataType::kDataTypeFP32 : DataType::kDataTypeFP16;
+    const SafetensorInfo* info = r.get_info(name);
+    double best = 1e30;
+    for (int i = 0; i < std::max(1, reps); ++i) {
+        const auto t0 = std::chrono::steady_clock::now();
+        auto t = r.get_tensor_gpu(name, alloc, dt);  // synchronous: data on the device at return
+        const auto t1 = std::chrono::steady_clock::now();
+        if (!t) {
+            std::cout << "r null\n";
+            return 0;
+        }
+        best = std::min(best, std::chrono::duration<double, std::milli>(t1 - t0).count());
+    }
+    std::cout << "time " << best << " " << (info->offset_end - info->offset_begin) << "\n";
+    return 0;
+}
+
 static std::shared_ptr<Tensor> upload_file(const std::shared_ptr<CUDAAllocator>& alloc, const std::string& path,
                                            std::vector<int> shape, DataType dt)
 {
@@ -291,6 +320,7 @@ int main(int argc, char** argv)
     if (cmd == "multi") return cmd_multi(argv[2], argc - 3, argv + 3);
     if (cmd == "config") return cmd_config(argv[2]);
     if (cmd == "json") return cmd_json(argv[2]);
+    if (cmd == "time" && argc == 6) return cmd_time(argv[2], argv[3], argv[4], std::atoi(argv[5]));
     if (cmd == "fetch" && argc >= 4) return cmd_fetch(argv[2], argv[3], argc - 4, argv + 4);
     if (cmd == "layers" && argc == 5) return cmd_layers(argv[2], argv[3], std::atoi(argv[4]));
     std::cerr << "bad arguments\n";
