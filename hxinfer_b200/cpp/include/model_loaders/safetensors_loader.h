@@ -60,7 +60,9 @@ public:
     // on the device.  Pairs: F32/F16/BF16 -> FP16 or FP32, I8 -> Int8.
     // nullptr (message on stderr) if the tensor is absent, the pair is not
     // supported, or an allocation or CUDA call fails.  Synchronous: the data
-    // is in place when the call returns.
+    // is in place when the call returns.  One reader serves one thread at a
+    // time (its staging buffers are shared between calls), as the reference's
+    // reader does.
     std::shared_ptr<Tensor> get_tensor_gpu(const std::string& name,
                                            const std::shared_ptr<CUDAAllocator>& alloc,
                                            DataType target_dtype = DataType::kDataTypeFP16) const;

@@ -5,15 +5,18 @@
 // RFC 8259 grammar: objects, arrays, strings with escapes (\uXXXX and
 // surrogate pairs to UTF-8), numbers, true/false/null.  Integers without a
 // fraction or exponent are kept exactly as int64 (safetensors byte offsets);
-// other numbers as double.  Nesting is limited to 64 levels.  Errors carry the
-// byte offset.  Object members keep their order; lookups are linear, which is
-// fine for these small documents.
+// other numbers as double, converted with std::from_chars so that the host
+// program's numeric locale (a comma decimal separator) cannot change them;
+// magnitudes past the double range become +-infinity or +-0.  Nesting is
+// limited to 64 levels.  Errors carry the byte offset.  Object members keep
+// their order; lookups are linear, which is fine for these small documents.
 #ifndef HXINFER_B200_JSON_LITE_H
 #define HXINFER_B200_JSON_LITE_H
-#include <cerrno>
+#include <charconv>
 #include <cstdint>
-#include <cstdlib>
+#include <limits>
 #include <string>
+#include <system_error>
 #include <utility>
 #include <vector>
 
@@ -265,14 +268,24 @@ private:
             if (p_ >= end_ || *p_ < '0' || *p_ > '9') return set("digit expected in exponent");
             while (p_ < end_ && *p_ >= '0' && *p_ <= '9') ++p_;
         }
-        const std::string tok(start, p_);
         v.kind = Value::Number;
-        errno = 0;
-        v.number = std::strtod(tok.c_str(), nullptr);
+        double d = 0.0;
+        const auto r = std::from_chars(start, p_, d);
+        if (r.ec == std::errc::result_out_of_range) {
+            // past the double range: an exponent below zero underflows, else overflow
+            bool neg_exp = false;
+            for (const char* q = start; q < p_; ++q)
+                if (*q == 'e' || *q == 'E') neg_exp = q + 1 < p_ && q[1] == '-';
+            d = neg_exp ? 0.0 : std::numeric_limits<double>::infinity();
+            if (*start == '-') d = -d;
+        } else if (r.ec != std::errc() || r.ptr != p_) {
+            return set("malformed number");
+        }
+        v.number = d;
         if (integral) {
-            errno = 0;
-            const long long i = std::strtoll(tok.c_str(), nullptr, 10);
-            if (errno == 0) {
+            long long i = 0;
+            const auto ri = std::from_chars(start, p_, i);
+            if (ri.ec == std::errc() && ri.ptr == p_) {
                 v.is_int = true;
                 v.integer = (int64_t)i;
             }

@@ -292,3 +292,16 @@ def test_json_reader_keeps_int64_exact(loader_bin, tmp_path):
     assert out[0] == "ok 9223372036854775807" and out[1] == "ok -9223372036854775808"
     assert out[2] == "ok [0,0,1.8446744073709552e+19]"  # past int64: a double
     assert out[3] == 'ok {"data_offsets":[4294967296,1099511627776]}'
+
+
+def test_json_reader_numbers_at_the_double_range_edges(loader_bin, tmp_path):
+    docs = ["5e-324", "1e-310", "-4.9406564584124654e-324", "2.2250738585072014e-308",
+            "1.7976931348623157e308", "0.1", "-0.0", "1E+2", "123456789012345678901234"]
+    out = _json_lines(loader_bin, tmp_path, docs)
+    for d, line in zip(docs, out):
+        want = json.loads(d)
+        if isinstance(want, int) and not -2**63 <= want < 2**63:
+            want = float(want)  # integers past int64 become the nearest double
+        assert line.startswith("ok ") and json.loads(line[3:]) == want, (d, line)
+    over = _json_lines(loader_bin, tmp_path, ["1e999", "-1e999", "1e-400", "-1e-400"])
+    assert over == ["ok inf", "ok -inf", "ok 0", "ok -0"]
