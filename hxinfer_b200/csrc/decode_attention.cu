@@ -891,15 +891,15 @@ static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas
 {
     auto kernel = decode_attention_kernel<ROWS, STAGES, CTAS_PER_SM>;
     const size_t smem = sizeof(DecodeSmem<ROWS, STAGES>) + 1024;
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // per device; set again on ordinals past 63
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
         HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                          (int)cudaSharedmemCarveoutMaxShared));
-        attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
     cudaError_t e = launch_kernel(kernel, dim3(n_ctas), dim3(kDecThreads), smem, stream, ov,

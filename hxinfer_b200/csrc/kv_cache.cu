@@ -64,14 +64,17 @@ int* status_word()
 
 int num_sms()
 {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];  // zero = not yet read
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    if (dev >= 0 && dev < 64) {
+        const int c = cached[dev].load(std::memory_order_relaxed);
+        if (c) return c;
+    }
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
-    if (dev >= 0 && dev < 64) cached[dev] = n;
+    if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 

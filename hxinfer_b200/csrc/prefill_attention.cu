@@ -473,13 +473,13 @@ extern "C" int hx_prefill_attention(const hx_kv_cache* c, int layer, const void*
     p.out_f32 = out_dtype == HX_FP32;
     p.status = status_word();
     const size_t smem = sizeof(PrefillSmem) + 1024;
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // per device; set again on ordinals past 63
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         HX_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     dim3 grid(num_q_heads, p.n_qtiles);
     prefill_attention_kernel<<<grid, kPfThreads, smem, (cudaStream_t)stream>>>(tm_q, c->tm_k, c->tm_v, p);

@@ -349,13 +349,13 @@ static int launch_qkv(const hx_kv_cache* c, const KVView& view, const void* x, i
                   : variant == 1 ? qkv_rope_append_kernel<NTOK, kBigBatch, TP, TO>
                                  : qkv_rope_append_kernel<NTOK, kSmallBatch, TP, TO>;
     const size_t smem = (size_t)(mma ? 8 : NTOK) * hidden * 2;
-    static bool attr_set[64][3] = {};
+    static std::atomic<bool> attr_set[64][3];  // per device; set again on ordinals past 63
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev][variant]) {
+    if (dev < 0 || dev >= 64 || !attr_set[dev][variant].load(std::memory_order_acquire)) {
         HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (mma ? 8 : NTOK) * 8192 * 2));
-        attr_set[dev][variant] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev][variant].store(true, std::memory_order_release);
     }
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
     cudaError_t e = launch_kernel(
