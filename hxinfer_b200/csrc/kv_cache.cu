@@ -255,7 +255,11 @@ extern "C" int hx_device_status(int clear)
     HX_CUDA_TRY(cudaDeviceSynchronize());
     int v = 0;
     HX_CUDA_TRY(cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost));
-    if (clear) HX_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+    if (clear) {
+        HX_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+        // the reset must land before later launches on non-blocking streams run
+        HX_CUDA_TRY(cudaDeviceSynchronize());
+    }
     if (v != HX_OK) fail(v, "a kernel recorded: %s", hx_status_string(v));
     return v;
 }
