@@ -85,17 +85,19 @@ class ClockSampler:
         self.uuids = set(uuids)
         self.proc = None
         self.path = None
+        self.out = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
+        self.out = open(self.path, "w")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "--query-gpu=uuid,clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
                  "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         time.sleep(0.3)
@@ -108,6 +110,9 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+                self.proc.wait()
+        if self.out:
+            self.out.close()
 
     def summary(self):
         sm, mx, reasons = [], [], set()
