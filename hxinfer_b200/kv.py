@@ -309,22 +309,33 @@ class PeerGather:
         check(lib.hx_dist_create(rank, world, buffer_bytes, C.byref(h)), "dist create")
         self.handle = h
         self.rank, self.world, self.bytes = rank, world, buffer_bytes
-        n = int(lib.hx_dist_handle_bytes())
-        mine = (C.c_char * n)()
-        check(lib.hx_dist_export(self.handle, mine), "dist export")
-        blobs = exchange(bytes(mine))
-        if len(blobs) != world or any(len(b) != n for b in blobs):
-            raise ValueError("exchange must return one handle per rank")
-        allh = (C.c_char * (n * world)).from_buffer_copy(b"".join(blobs))
-        check(lib.hx_dist_connect(self.handle, allh), "dist connect")
+        try:
+            n = int(lib.hx_dist_handle_bytes())
+            mine = (C.c_char * n)()
+            check(lib.hx_dist_export(self.handle, mine), "dist export")
+            blobs = exchange(bytes(mine))
+            if len(blobs) != world or any(len(b) != n for b in blobs):
+                raise ValueError("exchange must return one handle per rank")
+            allh = (C.c_char * (n * world)).from_buffer_copy(b"".join(blobs))
+            check(lib.hx_dist_connect(self.handle, allh), "dist connect")
+        except BaseException:
+            lib.hx_dist_destroy(self.handle)  # nothing of this rank is in use yet
+            self.handle = None
+            raise
         self.ptr = int(lib.hx_dist_buffer(self.handle))
 
     def view(self, dtype=torch.float16, offset: int = 0, shape=None) -> torch.Tensor:
-        """A tensor over this rank's buffer (no copy; valid while the endpoint lives)."""
+        """A tensor over this rank's buffer (no copy; valid while the endpoint
+        lives).  The view must lie inside the buffer."""
         esize = torch.empty((), dtype=dtype).element_size()
+        if offset < 0 or offset % esize or offset > self.bytes:
+            raise ValueError(f"offset {offset} outside the {self.bytes}-byte buffer or misaligned")
         numel = (self.bytes - offset) // esize
         if shape is not None:
             numel = math.prod(shape)
+            if offset + numel * esize > self.bytes:
+                raise ValueError(f"a {tuple(shape)} {dtype} view at offset {offset} does not fit "
+                                 f"the {self.bytes}-byte buffer")
         storage = torch.cuda.current_device()
         return _tensor_at(self.ptr + offset, numel, dtype, storage, self).view(
             *(shape if shape is not None else (numel,)))
@@ -336,9 +347,18 @@ class PeerGather:
         check(load().hx_dist_wait(self.handle, epoch & 0xFFFFFFFF, _stream(stream)), "dist wait")
 
     def close(self):
+        """Releases the endpoint.  Synchronise and pass a host barrier first:
+        peers may still be writing into this rank's buffer until they have
+        waited for the last epoch."""
         if getattr(self, "handle", None):
             check(load().hx_dist_destroy(self.handle), "dist destroy")
             self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _tensor_at(ptr: int, numel: int, dtype, device: int, owner) -> torch.Tensor:

@@ -106,3 +106,15 @@ def test_assemble_with_a_rank_without_sequences():
     part1 = np.zeros((0, 32), np.float32)
     out = D.assemble(mode, [part0, part1], shards, 1, 8, 4)
     assert np.array_equal(out, part0)
+
+
+def test_peer_gather_views_must_fit_the_buffer():
+    """View arguments are checked on the host before any device pointer is
+    used (an out-of-bounds view of peer-mapped memory would fault on use)."""
+    import torch
+    from hxinfer_b200 import kv
+    pg = kv.PeerGather.__new__(kv.PeerGather)  # no endpoint: only the checks run
+    pg.bytes, pg.ptr, pg.handle = 1024, 0, None
+    for offset, shape in ((0, (513,)), (1000, (16,)), (-2, None), (1, None), (2048, None)):
+        with pytest.raises(ValueError):
+            pg.view(torch.float16, offset, shape)
