@@ -3,9 +3,10 @@
 Every kernel source is compiled with the library's own flags plus
 `-Xptxas -v` into a scratch directory.  Every kernel entry point must
 report no spill stores or loads: a spill in a hot kernel is a silent
-performance regression.  Registers per thread must stay at or below 255;
-the register budgets that the launch bounds imply (threads x minimum CTAs
-per SM) are enforced by ptxas itself, which fails the build otherwise.
+performance regression.  ptxas caps each kernel's registers at the budget
+its launch bounds imply (threads x minimum CTAs per SM) and spills past it,
+so the spill check also guards those budgets; registers per thread must
+stay at or below 255.
 """
 import os
 import re
