@@ -8,14 +8,19 @@
 // copies it back into the first prefix_len positions, leaving later positions
 // untouched; a restore miss prints an error and returns.
 //
-// What changes: snapshots live in device memory from `allocator` (one
-// buffer per layer holding K and V) and the copies are device kernels
-// (hx_kv_snapshot / hx_kv_restore) on the legacy default stream, ordered with
-// the model's own launches.  store/restore accept any model type whose
-// get_blocks()[i]->get_attention() yields this build's AttentionLayer
-// (LlamaModel, Qwen2Model, CausalLMModel).
+// What changes: the copies are device kernels (hx_kv_snapshot /
+// hx_kv_restore) on the legacy default stream, ordered with the model's own
+// launches, and each layer's K and V snapshot is one buffer from `allocator`.
+// With a device allocator (CUDAAllocator, DeviceAllocator) snapshots stay in
+// device memory.  With a CPUAllocator (what the reference's callers pass: its
+// snapshots are host tensors) they stay in host memory, as in the reference,
+// and move through a device staging buffer with a synchronous cudaMemcpy.
+// store/restore accept any model type whose get_blocks()[i]->get_attention()
+// yields this build's AttentionLayer (LlamaModel, Qwen2Model, CausalLMModel).
 #ifndef HXINFER_B200_PREFIX_CACHE_H
 #define HXINFER_B200_PREFIX_CACHE_H
+#include <cuda_runtime.h>
+
 #include <cstdint>
 #include <iostream>
 #include <memory>
@@ -40,6 +45,21 @@ private:
     std::unordered_map<size_t, std::shared_ptr<CachedKVBlock>> cache_map_;
     std::shared_ptr<Allocator> allocator_;
     ModelConfig config_;
+    std::shared_ptr<Tensor> staging_;  // device copy of one layer's snapshot (host snapshots)
+
+    bool host_snapshots() const
+    {
+        return allocator_ && allocator_->device_type() == DeviceType::kDeviceCPU;
+    }
+    // Device buffer of at least `bytes` bytes for host-resident snapshots.
+    void* staging(size_t bytes)
+    {
+        if (!staging_ || staging_->tensor_total_byte_size() < bytes)
+            staging_ = std::make_shared<Tensor>(std::make_shared<CUDAAllocator>(),
+                                                std::vector<int>{static_cast<int>(bytes)},
+                                                DataType::kDataTypeInt8);
+        return staging_->raw_data_ptr();
+    }
 
     size_t compute_hash(const std::vector<int>& tokens) const
     {
@@ -65,9 +85,24 @@ public:
             auto snap = std::make_shared<Tensor>(
                 allocator_, std::vector<int>{static_cast<int>(bytes > 0 ? bytes : 1)},
                 DataType::kDataTypeInt8);
-            int rc = hx_kv_snapshot(kv, 0, prefix_len, snap->raw_data_ptr(), bytes, nullptr);
+            if (!snap->raw_data_ptr()) {
+                std::cerr << "[PrefixCache] store failed: snapshot allocation of " << bytes
+                          << " bytes" << std::endl;
+                return;
+            }
+            int rc;
+            if (host_snapshots() && bytes > 0) {
+                void* dev = staging(bytes);
+                rc = dev ? hx_kv_snapshot(kv, 0, prefix_len, dev, bytes, nullptr) : HX_ERR_OOM;
+                if (rc == HX_OK &&
+                    cudaMemcpy(snap->raw_data_ptr(), dev, bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+                    rc = HX_ERR_CUDA;
+            } else {
+                rc = hx_kv_snapshot(kv, 0, prefix_len, snap->raw_data_ptr(), bytes, nullptr);
+            }
             if (rc != HX_OK) {
-                std::cerr << "[PrefixCache] store failed: " << hx_last_error() << std::endl;
+                std::cerr << "[PrefixCache] store failed: " << hx_status_string(rc) << " ("
+                          << hx_last_error() << ")" << std::endl;
                 return;
             }
             block->layer_kv.push_back(snap);
@@ -97,10 +132,22 @@ public:
         for (int i = 0; i < config_.layer; i++) {
             hx_kv_cache* kv = blocks[i]->get_attention()->kv_cache();
             const auto& snap = block->layer_kv[i];
-            int rc = hx_kv_restore(kv, 0, block->prefix_len, snap->raw_data_ptr(),
+            const size_t bytes = hx_snapshot_bytes(kv, block->prefix_len);
+            int rc;
+            if (host_snapshots() && bytes > 0) {
+                void* dev = staging(bytes);
+                rc = dev ? HX_OK : HX_ERR_OOM;
+                if (rc == HX_OK &&
+                    cudaMemcpy(dev, snap->raw_data_ptr(), bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+                    rc = HX_ERR_CUDA;
+                if (rc == HX_OK) rc = hx_kv_restore(kv, 0, block->prefix_len, dev, bytes, nullptr);
+            } else {
+                rc = hx_kv_restore(kv, 0, block->prefix_len, snap->raw_data_ptr(),
                                    snap->tensor_total_byte_size(), nullptr);
+            }
             if (rc != HX_OK) {
-                std::cerr << "[PrefixCache] restore failed: " << hx_last_error() << std::endl;
+                std::cerr << "[PrefixCache] restore failed: " << hx_status_string(rc) << " ("
+                          << hx_last_error() << ")" << std::endl;
                 return;
             }
         }

@@ -121,6 +121,22 @@ extern "C" size_t hx_snapshot_bytes(const hx_kv_cache* c, int prefix_len)
     return (size_t)c->cfg.num_layers * 2 * c->cfg.num_kv_heads * prefix_len * c->cfg.head_dim * 2;
 }
 
+// The copy kernels read and write the snapshot buffer directly: it must be
+// device, managed or mapped pinned memory.  A pageable host pointer would be
+// an illegal address on the device, so it is refused here, before any launch.
+static int check_device_accessible(const void* p)
+{
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();  // the query's error is not sticky: clear it for later calls
+        return fail(HX_ERR_INVALID, "snapshot buffer is not memory the device can address");
+    }
+    if (a.type == cudaMemoryTypeUnregistered || (a.type == cudaMemoryTypeHost && !a.devicePointer))
+        return fail(HX_ERR_INVALID, "snapshot buffer is pageable host memory; pass device, managed "
+                                    "or mapped pinned memory");
+    return HX_OK;
+}
+
 static int check_snapshot_args(const hx_kv_cache* c, int seq, int prefix_len, const void* buf,
                                size_t bytes)
 {
@@ -136,6 +152,7 @@ static int check_snapshot_args(const hx_kv_cache* c, int seq, int prefix_len, co
         return fail(HX_ERR_INVALID, "snapshot buffer of %zu bytes < %zu needed", bytes,
                     hx_snapshot_bytes(c, prefix_len));
     if (reinterpret_cast<uintptr_t>(buf) & 15) return fail(HX_ERR_INVALID, "snapshot buffer not 16-byte aligned");
+    if (prefix_len > 0) return check_device_accessible(buf);
     return HX_OK;
 }
 

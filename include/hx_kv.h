@@ -319,6 +319,8 @@ size_t hx_snapshot_bytes(const hx_kv_cache* cache, int prefix_len);
 
 /* K4: copies positions [0, prefix_len) of every layer's K and V of `seq` into
  * dst (device, layout [layer][K|V][kv_head][prefix_len][head_dim] fp16).
+ * dst (and src of hx_kv_restore) must be device, managed or mapped pinned
+ * memory; pageable host memory is refused with HX_ERR_INVALID.
  * Replaces the host memcpy of PrefixCacheManager::store (prefix_cache.h:78-89). */
 int hx_kv_snapshot(const hx_kv_cache* cache, int seq, int prefix_len, void* dst,
                    size_t dst_bytes, hx_stream_t stream);

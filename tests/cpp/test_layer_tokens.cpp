@@ -11,7 +11,8 @@
 // each path runs: n <= 8 with fp16 weights (fused projection), larger n
 // (cuBLAS GEMMs), head_dim 128 (tcgen05 prefill) and 64 (one decode call per
 // token), chunks crossing 64-position blocks, and a cache filled to a
-// capacity that is not a multiple of 64.  Exit status = number of failures.
+// capacity that is not a multiple of 64.  Also PrefixCacheManager with host
+// snapshots over caches filled that way.  Exit status = number of failures.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -21,9 +22,27 @@
 #include <string>
 #include <vector>
 
+#include "cache/prefix_cache.h"
 #include "hx_oracle.h"
 #include "layer/attention.h"
 #include "test_common.h"
+
+static std::vector<uint16_t> read_cache_bits(const std::shared_ptr<Tensor>& t)
+{
+    std::vector<uint16_t> h(t->tensor_total_byte_size() / 2);
+    cudaMemcpy(h.data(), t->raw_data_ptr(), t->tensor_total_byte_size(), cudaMemcpyDeviceToHost);
+    return h;
+}
+
+// A model-shaped holder: get_blocks()[i]->get_attention(), as LlamaModel has.
+struct Block {
+    std::shared_ptr<AttentionLayer> attn;
+    std::shared_ptr<AttentionLayer>& get_attention() { return attn; }
+};
+struct MiniModel {
+    std::vector<std::shared_ptr<Block>> blocks;
+    std::vector<std::shared_ptr<Block>>& get_blocks() { return blocks; }
+};
 
 static void test_tokens(int Hq, int Hkv, int hd, bool bias, bool fp16_weights, int seq_len,
                         const std::vector<int>& chunks)
@@ -158,6 +177,76 @@ static void test_shape_errors()
     CHECK_TRUE(threw, "input that is not [n, dim] is refused");
 }
 
+// PrefixCacheManager given a CPUAllocator, as the reference's callers construct
+// it (its snapshots are host tensors): snapshots stay in host memory and the
+// restore semantics are the same as with device snapshots.  The caches are
+// filled by multi-token forward calls.
+static void test_prefix_cache_host_snapshots()
+{
+    std::cout << "=== test_prefix_cache_host_snapshots (2 layers, 4/2 heads) ===" << std::endl;
+    const int Hq = 4, Hkv = 2, hd = 128, dim = Hq * hd, kv_dim = Hkv * hd, seq_len = 160;
+    const int n_fill = 150, plen = 131;
+    std::mt19937_64 g(17);
+    ModelConfig config{};
+    config.dim = dim;
+    config.head = Hq;
+    config.kv_head = Hkv;
+    config.layer = 2;
+    config.seq_len = seq_len;
+    config.rope_theta = 1e4f;
+    config.weight_dtype = DataType::kDataTypeFP32;
+    config.activation_dtype = DataType::kDataTypeFP32;
+    MiniModel model;
+    std::vector<std::shared_ptr<Tensor>> keep;
+    for (int l = 0; l < 2; l++) {
+        auto wq = cuda_f32(normal_f16(g, (size_t)dim * dim, 0.05f), {dim, dim});
+        auto wk = cuda_f32(normal_f16(g, (size_t)kv_dim * dim, 0.05f), {kv_dim, dim});
+        auto wv = cuda_f32(normal_f16(g, (size_t)kv_dim * dim, 0.05f), {kv_dim, dim});
+        auto wo = cuda_f32(normal_f16(g, (size_t)dim * dim, 0.05f), {dim, dim});
+        keep.insert(keep.end(), {wq, wk, wv, wo});
+        auto b = std::make_shared<Block>();
+        b->attn = std::make_shared<AttentionLayer>(cuda_alloc, config, wq, wk, wv, wo);
+        model.blocks.push_back(b);
+    }
+    auto fill = [&]() {  // positions 0 .. n_fill-1 in one call per layer
+        auto in = cuda_f32(normal_f16(g, (size_t)n_fill * dim), {n_fill, dim});
+        auto out = cuda_f32(std::vector<float>((size_t)n_fill * dim, 0.0f), {n_fill, dim});
+        for (auto& b : model.blocks) b->attn->forward(in, out, 0);
+    };
+    fill();
+    std::vector<std::vector<uint16_t>> snapK, snapV, overK, overV;
+    for (auto& b : model.blocks) {
+        snapK.push_back(read_cache_bits(b->attn->get_k_cache()));
+        snapV.push_back(read_cache_bits(b->attn->get_v_cache()));
+    }
+    std::vector<int> prefix(plen);
+    for (int i = 0; i < plen; i++) prefix[i] = static_cast<int>(g() % 152064);
+    PrefixCacheManager mgr(std::make_shared<CPUAllocator>(), config);
+    mgr.store(prefix, model);
+    fill();  // overwrite every cached position
+    for (auto& b : model.blocks) {
+        overK.push_back(read_cache_bits(b->attn->get_k_cache()));
+        overV.push_back(read_cache_bits(b->attn->get_v_cache()));
+    }
+    CHECK_TRUE(mgr.lookup(prefix) == plen && mgr.cache_size() == 1, "host snapshot stored and found");
+    mgr.restore(prefix, model);
+    for (int l = 0; l < 2; l++) {
+        auto k = read_cache_bits(model.blocks[l]->attn->get_k_cache());
+        auto v = read_cache_bits(model.blocks[l]->attn->get_v_cache());
+        bool ok = true;
+        for (int h = 0; h < Hkv; h++)
+            for (int p = 0; p < seq_len; p++)
+                for (int d = 0; d < hd; d++) {
+                    const size_t i = ((size_t)h * seq_len + p) * hd + d;
+                    const auto& wk = p < plen ? snapK[l] : overK[l];
+                    const auto& wv = p < plen ? snapV[l] : overV[l];
+                    ok = ok && k[i] == wk[i] && v[i] == wv[i];
+                }
+        CHECK_TRUE(ok, "host snapshot restore: first prefix_len positions back, later untouched (layer "
+                           << l << ")");
+    }
+}
+
 int main()
 {
     // head_dim 128: fused projection for n <= 8 (fp16 weights), GEMMs above, tcgen05 prefill
@@ -169,6 +258,7 @@ int main()
     // head_dim 64: no tcgen05 prefill; one decode call per token
     test_tokens(4, 2, 64, true, true, 512, {1, 6, 70, 3, 150});
     test_shape_errors();
+    test_prefix_cache_host_snapshots();
     cudaError_t e = cudaDeviceSynchronize();
     int st = hx_device_status(1);
     CHECK_TRUE(e == cudaSuccess, "no CUDA error (" << cudaGetErrorString(e) << ")");

@@ -7,7 +7,8 @@ one-token loop.  Appended K/V rows bit-exact (exact signed-permutation
 projections); outputs within 2e-3 + 1e-2 |ref|.  Covers the fused projection
 (n <= 8, fp16 weights), cuBLAS GEMMs, tcgen05 prefill (head_dim 128), one decode
 call per token (head_dim 64), a capacity that is not a multiple of 64 filled to the
-end, and shape errors.  Collected after the other GPU tests, so that a stop
+end, shape errors, and PrefixCacheManager with host-resident snapshots (a
+CPUAllocator, as the reference's callers pass) over caches filled that way.  Collected after the other GPU tests, so that a stop
 at the first failure has already run them.
 """
 import os
