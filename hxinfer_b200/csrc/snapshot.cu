@@ -123,13 +123,16 @@ extern "C" size_t hx_snapshot_bytes(const hx_kv_cache* c, int prefix_len)
 
 // The copy kernels read and write the snapshot buffer directly: it must be
 // device, managed or mapped pinned memory.  A pageable host pointer would be
-// an illegal address on the device, so it is refused here, before any launch.
+// an illegal address on the device, so one that the runtime reports as
+// unregistered (or as pinned but unmapped) host memory is refused here,
+// before any launch.  A pointer the query cannot classify is passed on as
+// before.
 static int check_device_accessible(const void* p)
 {
     cudaPointerAttributes a{};
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
         cudaGetLastError();  // the query's error is not sticky: clear it for later calls
-        return fail(HX_ERR_INVALID, "snapshot buffer is not memory the device can address");
+        return HX_OK;
     }
     if (a.type == cudaMemoryTypeUnregistered || (a.type == cudaMemoryTypeHost && !a.devicePointer))
         return fail(HX_ERR_INVALID, "snapshot buffer is pageable host memory; pass device, managed "
