@@ -141,6 +141,7 @@ using namespace hx;
 extern "C" int hx_convert(void* dst, int dst_dtype, const void* src, int src_dtype, size_t n,
                           hx_stream_t stream_)
 {
+    HX_NVTX_RANGE("hx_convert");
     const int sb = elem_bytes(src_dtype), db = elem_bytes(dst_dtype);
     if (!sb || !db || dst_dtype == HX_BF16)
         return fail(HX_ERR_INVALID, "hx_convert: unsupported dtypes %d -> %d", src_dtype, dst_dtype);

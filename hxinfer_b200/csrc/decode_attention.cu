@@ -1003,6 +1003,7 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
                                    int num_q_heads, float scale, void* out, int out_dtype,
                                    void* workspace, size_t workspace_bytes, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_decode_attention");
     if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
                                  out_dtype))
         return rc;
@@ -1032,6 +1033,7 @@ extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const
                                           int out_head0, int out_dtype, void* workspace,
                                           size_t workspace_bytes, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_decode_attention_gather");
     if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
                                  out_dtype))
         return rc;
@@ -1125,6 +1127,7 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
                                            float scale, void* out, int out_dtype,
                                            hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_decode_attention_noalloc");
     if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
                                  out_dtype))
         return rc;

@@ -177,6 +177,7 @@ extern "C" void* hx_dist_buffer(const hx_dist* d) { return d ? d->buf : nullptr;
 
 extern "C" int hx_dist_wait(hx_dist* d, uint32_t epoch, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_dist_wait");
     if (!d || !d->connected) return fail(HX_ERR_INVALID, "gather endpoint is not connected");
     if (d->world == 1) return HX_OK;
     PeerFlags peers{};

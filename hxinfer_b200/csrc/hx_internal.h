@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <nvtx3/nvToolsExt.h>
 #include <string>
 #include <vector>
 
@@ -95,3 +96,16 @@ KVView make_view(const hx_kv_cache* c, int layer);
         cudaError_t _e = (expr);                                     \
         if (_e != cudaSuccess) return hx::cuda_fail(_e, #expr);      \
     } while (0)
+
+namespace hx {
+// An NVTX range named after the C ABI call it covers: the call shows on a
+// profiler's timeline and `ncu --nvtx --nvtx-include "<name>/"` selects its
+// kernels.  Without a tool attached a push/pop is one pointer check.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+}  // namespace hx
+#define HX_NVTX_RANGE(name) ::hx::NvtxRange hx_nvtx_range_(name)

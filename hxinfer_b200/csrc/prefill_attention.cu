@@ -441,6 +441,7 @@ extern "C" int hx_prefill_attention(const hx_kv_cache* c, int layer, const void*
                                     int start, int n, int num_q_heads, float scale, void* out,
                                     int out_dtype, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_prefill_attention");
     if (!c) return fail(HX_ERR_INVALID, "null cache");
     if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
     if (!q || !out) return fail(HX_ERR_INVALID, "null q/out");

@@ -398,6 +398,7 @@ extern "C" int hx_qkv_rope_append(hx_kv_cache* c, int layer, const void* x, int 
                                   int num_q_heads, const hx_rope_table* table, void* q_out,
                                   int q_out_dtype, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_qkv_rope_append");
     if (!c) return fail(HX_ERR_INVALID, "null cache");
     if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
     if (c->cfg.head_dim != 128)

@@ -142,6 +142,7 @@ extern "C" int hx_rope_append(hx_kv_cache* c, int layer, const void* q, const vo
                               int n_tokens, int num_q_heads, const hx_rope_table* table,
                               void* q_out, int q_out_dtype, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_rope_append");
     if (!c) return fail(HX_ERR_INVALID, "null cache");
     if (layer < 0 || layer >= c->cfg.num_layers) return fail(HX_ERR_INVALID, "layer %d out of range", layer);
     if (!k || !v || !seq_ids || !positions) return fail(HX_ERR_INVALID, "null k/v/seq_ids/positions");
@@ -198,6 +199,7 @@ extern "C" int hx_rope_qk(void* q, void* k, int dtype, int rows, int num_q_heads
                           int num_kv_heads, int head_dim, int step, const hx_rope_table* table,
                           hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_rope_qk");
     if (!q || !k || !table) return fail(HX_ERR_INVALID, "null q/k/table");
     if (rows < 0 || num_q_heads < 1 || num_kv_heads < 1) return fail(HX_ERR_INVALID, "bad shape");
     if (head_dim != table->cfg.head_dim)

@@ -162,6 +162,7 @@ static int check_snapshot_args(const hx_kv_cache* c, int seq, int prefix_len, co
 extern "C" int hx_kv_snapshot(const hx_kv_cache* c, int seq, int prefix_len, void* dst,
                               size_t dst_bytes, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_kv_snapshot");
     if (int rc = check_snapshot_args(c, seq, prefix_len, dst, dst_bytes)) return rc;
     if (prefix_len == 0) return HX_OK;
     return launch_copy<true>(c, seq, prefix_len, dst, (cudaStream_t)stream);
@@ -170,6 +171,7 @@ extern "C" int hx_kv_snapshot(const hx_kv_cache* c, int seq, int prefix_len, voi
 extern "C" int hx_kv_restore(hx_kv_cache* c, int seq, int prefix_len, const void* src,
                              size_t src_bytes, hx_stream_t stream)
 {
+    HX_NVTX_RANGE("hx_kv_restore");
     if (int rc = check_snapshot_args(c, seq, prefix_len, src, src_bytes)) return rc;
     if (prefix_len == 0) return HX_OK;
     return launch_copy<false>(c, seq, prefix_len, const_cast<void*>(src), (cudaStream_t)stream);
