@@ -121,3 +121,33 @@ def test_header_is_c99_and_links_from_c(tmp_path):
                         "-o", str(tmp_path / "a.out"),
                         f"-L{pkg}", "-lhxkv", f"-Wl,-rpath,{pkg}"], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-3000:]
+
+
+def test_every_entry_point_refuses_null_arguments(hxlib):
+    """Each function of the ABI called with null pointers and zero sizes and
+    ids returns a status (or a benign value) instead of crashing, and none
+    needs a device to do so."""
+    import ctypes as C
+    from hxinfer_b200 import _lib
+    statuses = {}
+    for name, (restype, argtypes) in sorted(_lib.SIGNATURES.items()):
+        args = []
+        for a in argtypes:
+            if a in (C.c_float, C.c_double):
+                args.append(1.0)
+            elif a in (C.c_uint32,):
+                args.append(1)
+            elif a in (C.c_int, C.c_int32, C.c_int64, C.c_size_t, C.c_uint64):
+                args.append(0)
+            else:
+                args.append(None)
+        statuses[name] = getattr(hxlib, name)(*args)
+    int_status = {n: v for n, v in statuses.items() if _lib.SIGNATURES[n][0] is C.c_int}
+    # hx_device_status reads the device: HX_ERR_CUDA without one, HX_OK with one
+    assert int_status.pop("hx_device_status") in (_lib.HX_OK, _lib.HX_ERR_CUDA)
+    # destroying nothing succeeds; everything else refuses the null arguments
+    for n in ("hx_kv_destroy", "hx_dist_destroy", "hx_rope_table_destroy"):
+        assert int_status.pop(n) == _lib.HX_OK, n
+    bad = {n: v for n, v in int_status.items() if v != _lib.HX_ERR_INVALID}
+    assert not bad, bad
+    assert statuses["hx_decode_workspace_bytes"] == 0 and statuses["hx_snapshot_bytes"] == 0
