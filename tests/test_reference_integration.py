@@ -22,7 +22,8 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "hxinfer_b200")
-REFERENCE = os.environ.get("HXINFER_REFERENCE", "/root/reference")
+# the reference checkout: HXINFER_REFERENCE, else `reference` beside this repository
+REFERENCE = os.environ.get("HXINFER_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
 NVCC = "/usr/local/cuda/bin/nvcc"
 
 # this build's header -> the reference header it replaces (same relative path)
