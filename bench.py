@@ -10,7 +10,13 @@ aggregate decode tok/s; the decode kernel's achieved HBM GB/s is in
 ``roofline``.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload batched_decode|decode_32k|snapshot]
+                  [--collective p2p|nccl] [--overlap] [--no-cpu-baseline] [--no-c1-32k]
+
+At N=1 the same JSON line also carries ``c1_32k``: batch-1 decode on the
+Qwen2.5-7B attention shape (28 q heads, 4 kv heads, head_dim 128) over
+32,769 positions, 28 layers captured in one CUDA graph and timed as
+replays, with its microseconds per layer and its fraction of the measured
+HBM peak and of 8 TB/s.
 
 Multi-GPU (torchrun, one process per GPU, NCCL): at 8 GPUs each rank holds
 one kv head (4 q heads) of every sequence; at 2 or 4 GPUs each rank holds a
@@ -46,6 +52,8 @@ sys.path.insert(0, ROOT)
 
 SEED = 20261201
 HQ, HKV, HD, LAYERS, NSEQ = 32, 8, 128, 32, 64
+# One metric string for both arms, so the two lines can be compared directly.
+METRIC = "decode tok/s (batched decode attention)"
 # DRAM bytes (read + write) of one decode launch / its algorithmic bytes,
 # from an ncu capture of the same kernel on 16 sequences x 8192 positions
 # (540.6 MB of DRAM traffic for 537.0 MB of K+V+q+out); the traffic of the
@@ -177,20 +185,27 @@ def run_reference(args):
     for _ in range(args.warmup):
         cpu_decode_rate(lengths, 2, nthreads, min_seconds=0.0)
     descs = ""
+    sample_s = []
     for _ in range(args.steps):
-        r, descs, _ = cpu_decode_rate(lengths, 2, nthreads, min_seconds=1.0)
+        r, descs, t_sample = cpu_decode_rate(lengths, 2, nthreads, min_seconds=1.0)
         rates.append(r)
+        sample_s.append(t_sample)
     val = statistics.median(rates)
-    line = {"impl": "reference", "metric": "decode tok/s (batched decode attention)",
+    med_sample = statistics.median(sample_s)
+    line = {"impl": "reference", "metric": METRIC,
             "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * NSEQ / val,
+            "warmup": args.warmup,
+            # extrapolated: one sample covers 2 of the 64 sequences of 1 of the
+            # 32 layers; the time actually measured per sample is sample_ms
+            "ms_per_step": 1000.0 * NSEQ / val, "ms_per_step_kind": "extrapolated from sample_ms",
+            "sample_ms": 1000.0 * med_sample,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic N(0,1) K/V rounded to fp16",
             "config": {"workload": "batched_decode_llama3_8b_attention", "layers": LAYERS,
                        "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "sequences": NSEQ,
                        "lengths": "U[512,32768] seed 20261201"},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": nthreads, "kind": "port",
-                             "sample": descs},
+                             "sample": descs, "sample_ms": 1000.0 * med_sample},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -393,7 +408,7 @@ def run_batched_decode(args):
     tok_s = NSEQ * K / (ms * 1e-3)
     if rank == 0:
         line = {
-            "metric": "decode tok/s (batched decode attention; decode-kernel HBM GB/s in roofline)",
+            "metric": METRIC,
             "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 storage / f32 accumulate", "data": "synthetic",
@@ -417,10 +432,10 @@ def run_batched_decode(args):
             "cpu_baseline": cpu,
             "e2e": {"value": NSEQ * K / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": K * LAYERS * (4 if p2p else 3),
+            "gpu_launches": K * LAYERS * (1 + kv.decode_kernel_count(n * hkv, HD, HQ // HKV)
+                                          + (1 if p2p else 0)),
             "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()  # no rank unmaps its buffer while a peer may still write it
@@ -428,9 +443,91 @@ def run_batched_decode(args):
         peer.close()
     cache.close()
     table.close()
+    if rank == 0:
+        if world == 1 and not args.no_c1_32k:
+            del q_in, k_in, v_in, q_rot, out, q_d, k_d, v_d
+            torch.cuda.empty_cache()
+            line["c1_32k"] = run_c1_32k(args)
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_c1_32k(args, layers: int = 28, ctx: int = 32768, replays: int = 50):
+    """Batch-1 decode on the Qwen2.5-7B attention shape (28 q heads, 4 kv
+    heads, head_dim 128, RoPE theta 1e6): one new token appended at position
+    32768 and attended over 32,769 positions, for each of 28 layers.  The 28
+    layers are captured in one CUDA graph and timed as replays with CUDA
+    events; `decode_us_per_layer` is the decode call alone (q already
+    rotated), `step_us_per_layer` includes the fused RoPE + append.  The 28
+    layers hold 1.88 GB of K/V, so no layer's 67 MB is still in L2 when it
+    is read again."""
+    import torch
+
+    from hxinfer_b200 import kv
+
+    hq, hkv = 28, 4
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cap = ctx + 1
+    cache = kv.KVCache(layers, hkv, HD, 1, cap, overlap=True)
+    cache.reserve(0, cap)
+    cache.fill_normal(SEED + 32)
+    table = kv.RopeTable(HD, cap, 1e6)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 33)
+    q = torch.randn((layers, 1, hq * HD), generator=g, device=dev).half()
+    k = torch.randn((layers, 1, hkv * HD), generator=g, device=dev).half()
+    v = torch.randn((layers, 1, hkv * HD), generator=g, device=dev).half()
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+    sid = torch.zeros(1, dtype=torch.int32, device=dev)
+    pos = torch.full((1,), ctx, dtype=torch.int32, device=dev)
+    lens = pos + 1
+    ws = torch.zeros(cache.workspace_bytes(1, hq), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream()
+
+    def step(with_append):
+        for l in range(layers):
+            if with_append:
+                cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
+                                  q_out=q_rot[l], stream=stream)
+            cache.decode(l, q_rot[l], sid, lens, hq, out=out[l], workspace=ws, stream=stream)
+
+    res = {}
+    with torch.cuda.stream(stream):
+        step(True)  # kernel attributes are set outside the capture
+        torch.cuda.synchronize()
+        for name, app in (("decode", False), ("step", True)):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(app)
+            for _ in range(3):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(replays):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            res[name] = 1e3 * e0.elapsed_time(e1) / (replays * layers)
+            del graph
+    kv.device_status()
+    cache.close()
+    table.close()
+    kv_bytes = 2 * (ctx + 1) * hkv * HD * 2
+    dec_bytes = kv_bytes + 2 * hq * HD * 2                  # + q read, out write
+    step_bytes = dec_bytes + 2 * hkv * HD * 2 * 2 + hq * HD * 2 * 2  # + k/v in, row out, q in/out
+    peak, peak_kind = peaks()
+    dec_gbs = dec_bytes / (res["decode"] * 1e-6) / 1e9
+    return {"workload": "qwen2.5-7b attention, batch 1, 32769 positions, 28 layers, CUDA graph",
+            "decode_us_per_layer": res["decode"], "step_us_per_layer": res["step"],
+            "decode_bytes_per_layer": dec_bytes, "step_bytes_per_layer": step_bytes,
+            "decode_gbs": dec_gbs, "frac_measured_peak": dec_gbs / peak, "peak_kind": peak_kind,
+            "frac_8tbs": dec_gbs / 8000.0,
+            "target_us_per_layer": dec_bytes / (0.75 * 8000e9) * 1e6,
+            "step_gbs": step_bytes / (res["step"] * 1e-6) / 1e9,
+            "replays": replays, "launch": "programmatic dependent (HX_KV_OVERLAP_LAUNCH)"}
 
 
 def main():
@@ -439,9 +536,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="batched_decode",
-                    choices=["batched_decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c1-32k", action="store_true",
+                    help="skip the batch-1 Qwen 32k decode sub-record (N=1 only)")
     ap.add_argument("--overlap", action="store_true",
                     help="launch append and decode as programmatic dependents (HX_KV_OVERLAP_LAUNCH)")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
