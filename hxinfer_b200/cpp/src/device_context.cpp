@@ -88,7 +88,8 @@ void* workspace(size_t bytes)
         s.ws = nullptr;
         s.ws_bytes = 0;
         if (cudaMalloc(&s.ws, bytes) != cudaSuccess) return nullptr;
-        // zero-filled once; the decode kernels write every scratch word they read
+        // zero-filled once, as hx_decode_attention requires; every call leaves
+        // its counters zero again
         if (cudaMemset(s.ws, 0, bytes) != cudaSuccess) return nullptr;
         s.ws_bytes = bytes;
     }

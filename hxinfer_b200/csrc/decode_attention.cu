@@ -25,14 +25,18 @@
 //  * At the end of each piece (the part of a segment inside one CTA) the four
 //    warps merge in the shared memory of the stage they just consumed.  A
 //    piece that is a whole segment writes the normalised output; otherwise
-//    it writes (O, m, l) to a workspace slot and decode_combine_kernel (one
-//    CTA per segment and q row, launched as a programmatic dependent) merges
-//    the pieces by log-sum-exp.
+//    it writes (O, m, l) to a workspace slot, and the pieces are merged by
+//    log-sum-exp: in wide calls (few pieces per segment) by the CTA whose
+//    arrival completes the segment, counted in a per-segment counter; in
+//    narrow calls (batch 1: dozens of pieces per segment) by
+//    decode_combine_kernel, one CTA per segment and q row, launched as a
+//    programmatic dependent.
 //
-// Workspace: slot (seq*hkv + kv_head) holds the piece that starts at a
-// segment's first tile; slot (n_segments + c) holds CTA c's first piece when
-// that piece starts inside a segment, so slots = n_segments + C.  Every slot
-// the combine reads is written in the same call: nothing needs clearing.
+// Workspace: a fixed 64 KiB block of per-segment counters (zero between
+// calls), then the slots: slot (seq*hkv + kv_head) holds the piece that
+// starts at a segment's first tile; slot (n_segments + c) holds CTA c's first
+// piece when that piece starts inside a segment, so slots = n_segments + C.
+// Every slot a merge reads is written earlier in the same call.
 #include <cfloat>
 #include <mutex>
 
@@ -80,6 +84,10 @@ struct DecodeParams {
     float* ws_o;               // [slots][group][128]
     float2* ws_ml;             // [slots][group] (m, l)
     int* status;
+    // Folded combine (wide calls): one arrival counter per segment.  The CTA
+    // that completes a segment's last piece merges its pieces itself and
+    // returns the counter to zero; null = the separate combine kernel merges.
+    unsigned int* fold_cnt;
 };
 
 constexpr int kMinTilesPerCta = 2;  // small problems use fewer CTAs, hence fewer pieces
@@ -105,6 +113,8 @@ struct DecodeSmem {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     Sched sched;
+    int fold_ca;               // folded combine: first CTA of the segment to merge, or -1
+    int fold_np;               // and its number of pieces
     int cstart[kMaxPieces];    // first global tile of CTA c, c in [0, n_eff]
 };
 
@@ -148,9 +158,13 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
     const int hkv = p.view.hkv;
     long long total = 0;
     bool odd = false;
+    // The first 32 sequences' lengths and ids are loaded together and kept,
+    // so a call of up to 32 sequences plans with one round of global loads.
+    const int len0 = lane < p.n_seqs ? p.lengths[lane] : 1;
+    const int sid0 = lane < p.n_seqs ? p.seq_ids[lane] : 0;
     for (int base = 0; base < p.n_seqs; base += 32) {
         const int s = base + lane;
-        const int len = s < p.n_seqs ? p.lengths[s] : 1;
+        const int len = base == 0 ? len0 : (s < p.n_seqs ? p.lengths[s] : 1);
         odd |= len < 1 || len > p.view.capacity;
         int t = tiles_of(clamp_len(len, p.view.capacity)) * (s < p.n_seqs);
 #pragma unroll
@@ -184,8 +198,9 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
         int run = 0;  // tiles before the current chunk
         for (int base = 0; base < p.n_seqs; base += 32) {
             const int s = base + lane;
-            const int len = s < p.n_seqs ? clamp_len(p.lengths[s], p.view.capacity) : 0;
-            const int sid = s < p.n_seqs ? p.seq_ids[s] : 0;  // issued with the length load
+            const int len = s < p.n_seqs
+                ? clamp_len(base == 0 ? len0 : p.lengths[s], p.view.capacity) : 0;
+            const int sid = base == 0 ? sid0 : (s < p.n_seqs ? p.seq_ids[s] : 0);
             const int t = tiles_of(len) * hkv;
             int incl = t;
 #pragma unroll
@@ -299,6 +314,50 @@ __device__ void zero_empty_outputs(const DecodeParams& p)
     }
 }
 
+// Folded combine: merges the np pieces of segment `seg` (slot seg, then slot
+// n_seg + ca + k for k = 1 .. np-1, as the decode kernel writes them) by
+// log-sum-exp for every q row of the group, and writes the normalised rows
+// to dst ([group][128] fp32 in shared memory).  Warp w takes rows w, w + 4,
+// ...; lane i dims 4i .. 4i+3.  Loads go to L2 (the pieces come from other
+// SMs), four pieces at a time, merged online.
+__device__ void fold_merge_rows(const DecodeParams& p, int seg, int n_seg, int ca, int np,
+                                float* dst, int w, int lane)
+{
+    for (int r = w; r < p.group; r += kDecConsumerWarps) {
+        float M = -INFINITY, L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = 0; j0 < np; j0 += 4) {
+            float2 ml[4];
+            float4 ov[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int j = j0 + k;
+                ml[k] = make_float2(-INFINITY, 0.f);
+                ov[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j < np) {
+                    const int64_t slot = j == 0 ? seg : (int64_t)n_seg + ca + j;
+                    ml[k] = __ldcg(&p.ws_ml[slot * p.group + r]);
+                    ov[k] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (slot * p.group + r) * 128) + lane);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float Mn = fmaxf(M, ml[k].x);
+                const float Mu = Mn == -INFINITY ? 0.f : Mn;
+                const float a = fast_exp2(M - Mu), b = fast_exp2(ml[k].x - Mu);
+                L = L * a + ml[k].y * b;
+                acc.x = acc.x * a + ov[k].x * b;
+                acc.y = acc.y * a + ov[k].y * b;
+                acc.z = acc.z * a + ov[k].z * b;
+                acc.w = acc.w * a + ov[k].w * b;
+                M = Mn;
+            }
+        }
+        *reinterpret_cast<float4*>(dst + r * 128 + 4 * lane) =
+            make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
+    }
+}
+
 template <int ROWS, int STAGES, int CTAS_PER_SM>
 __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -341,42 +400,60 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
 
     if (warp == kDecConsumerWarps) {
         // ------------------------------------------------------------ producer
-        if (lane != 0) return;
-        prefetch_tensormap(&tm_k);
-        prefetch_tensormap(&tm_v);
+        // The whole warp walks the tiles (the cursor is uniform across
+        // lanes); lane 0 issues the copies.  Block-table entries come in
+        // windows of 32 consecutive blocks of one sequence, one coalesced
+        // load per window, so issuing the first ring of tiles costs one
+        // round of global loads instead of one per tile.
+        if (lane == 0) {
+            prefetch_tensormap(&tm_k);
+            prefetch_tensormap(&tm_v);
+        }
         const uint64_t pol = l2_evict_first_policy();
         const KVView& v = p.view;
         bool waited = false;
+        int win_seq = -1, win_j0 = 0;  // window: blocks [win_j0, win_j0 + 32) of win_seq
+        int64_t win_pb = -1;           // this lane's entry: block win_j0 + lane
         for (int i = 0; i < count; ++i) {
             const int st = i % kDecStages;
             const uint32_t round = (uint32_t)(i / kDecStages);
-            if (i >= kDecStages && !mbar_wait(&sm.empty[st], (round - 1) & 1)) {
-                record_status(p.status, HX_ERR_TIMEOUT);
+            bool ok = true;
+            if (lane == 0 && i >= kDecStages) ok = mbar_wait(&sm.empty[st], (round - 1) & 1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                if (lane == 0) record_status(p.status, HX_ERR_TIMEOUT);
                 return;
             }
             if (!waited && cur.j == cur.tiles - 1) {
                 pdl_wait();  // the segment's last tile holds the newest position
                 waited = true;
             }
-            const int64_t pb = phys_block(v, cur.seq, cur.j);
-            if (pb < 0) {
-                // unmapped block: no copy is issued; the consumers still get a
-                // completed phase (stale data) and the status word records it
-                record_status(p.status, HX_ERR_CAPACITY);
-                mbar_arrive(&sm.full[st]);
-            } else {
-                const int64_t rel = (pb * v.block_stride + (int64_t)cur.h * v.head_stride) / 256;
-                const int row_k = (int)(v.k_row0 + rel), row_v = (int)(v.v_row0 + rel);
-                mbar_arrive_expect_tx(&sm.full[st], kStageTxBytes);
-                uint8_t* kd = sm.stage[st][0];
-                uint8_t* vd = sm.stage[st][1];
-                tma_load_2d(kd, &tm_k, 0, row_k, &sm.full[st], pol);
-                tma_load_2d(kd + kHalfTileBytes, &tm_k, 64, row_k, &sm.full[st], pol);
-                tma_load_2d(vd, &tm_v, 0, row_v, &sm.full[st], pol);
-                tma_load_2d(vd + kHalfTileBytes, &tm_v, 64, row_v, &sm.full[st], pol);
+            if (cur.seq != win_seq || cur.j < win_j0 || cur.j >= win_j0 + 32) {
+                win_seq = cur.seq;
+                win_j0 = cur.j;
+                win_pb = phys_block(v, win_seq, win_j0 + lane);
+            }
+            const int64_t pb = __shfl_sync(0xffffffffu, win_pb, cur.j - win_j0);
+            if (lane == 0) {
+                if (pb < 0) {
+                    // unmapped block: no copy is issued; the consumers still get
+                    // a completed phase (stale data) and the status word records it
+                    record_status(p.status, HX_ERR_CAPACITY);
+                    mbar_arrive(&sm.full[st]);
+                } else {
+                    const int64_t rel = (pb * v.block_stride + (int64_t)cur.h * v.head_stride) / 256;
+                    const int row_k = (int)(v.k_row0 + rel), row_v = (int)(v.v_row0 + rel);
+                    mbar_arrive_expect_tx(&sm.full[st], kStageTxBytes);
+                    uint8_t* kd = sm.stage[st][0];
+                    uint8_t* vd = sm.stage[st][1];
+                    tma_load_2d(kd, &tm_k, 0, row_k, &sm.full[st], pol);
+                    tma_load_2d(kd + kHalfTileBytes, &tm_k, 64, row_k, &sm.full[st], pol);
+                    tma_load_2d(vd, &tm_v, 0, row_v, &sm.full[st], pol);
+                    tma_load_2d(vd + kHalfTileBytes, &tm_v, 64, row_v, &sm.full[st], pol);
+                }
             }
             cursor_next(cur, p);
         }
+        if (lane != 0) return;
         // Wait for the last copies to land before the CTA may exit.
         for (int i = count > kDecStages ? count - kDecStages : 0; i < count; ++i) {
             const int st = i % kDecStages;
@@ -614,6 +691,29 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
                 asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
                 store_rows(p, cur.s, cur.h * p.group, &merge_o[0][0][0], 128, p.group, d,
                            kDecConsumerWarps * 32);
+            } else if (p.fold_cnt) {
+                // Folded combine: count this piece in; the CTA that brings
+                // the segment's last piece merges all of its pieces.
+                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                if (threadIdx.x == 0) {
+                    const int a = g_first + i - cur.j;  // the segment's first global tile
+                    const int ca = cta_of_tile(sm.cstart, n_eff, a);
+                    const int np = cta_of_tile(sm.cstart, n_eff, a + cur.tiles - 1) - ca + 1;
+                    fence_acq_rel_gpu();  // this CTA's partials before the arrival
+                    const unsigned old = atomicInc(p.fold_cnt + seg, (unsigned)(np - 1));
+                    const bool last = old == (unsigned)(np - 1);  // the counter is back to 0
+                    if (last) fence_acq_rel_gpu();  // the other pieces after it
+                    sm.fold_ca = last ? ca : -1;
+                    sm.fold_np = np;
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                const int ca = sm.fold_ca;
+                if (ca >= 0) {
+                    fold_merge_rows(p, seg, n_seg, ca, sm.fold_np, &merge_o[0][0][0], w, lane);
+                    asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
+                    store_rows(p, cur.s, cur.h * p.group, &merge_o[0][0][0], 128, p.group, d,
+                               kDecConsumerWarps * 32);
+                }
             }
             fence_proxy_async_smem();  // the producer's next copy into this stage comes after
             asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
@@ -858,25 +958,37 @@ __global__ void __launch_bounds__(128)
     }
 }
 
+// Workspace layout: [fold counters][ws_o][ws_ml].  The counter block has the
+// same size in every workspace, whatever the call, so that no call's partial
+// results ever land on counters another call uses: the counters stay zero
+// between calls (the CTA that completes a segment returns its counter to
+// zero) once the workspace has been zero-filled before its first use.
+constexpr int kFoldMaxSegments = 16384;
+constexpr size_t kWsHeaderBytes = kFoldMaxSegments * sizeof(unsigned int);  // 64 KiB
+
 static size_t decode_ws_bytes(int n_seqs, int hkv, int group, int n_ctas)
 {
     const size_t slots = (size_t)n_seqs * hkv + n_ctas;
-    return slots * group * 128 * sizeof(float) + slots * group * sizeof(float2);
+    return kWsHeaderBytes + slots * group * 128 * sizeof(float) + slots * group * sizeof(float2);
 }
 
-// Layout of the workspace: [ws_o][ws_ml].
 static void bind_workspace(DecodeParams& p, void* ws, int n_ctas)
 {
     const size_t slots = (size_t)p.n_seqs * p.view.hkv + n_ctas;
-    char* base = static_cast<char*>(ws);
+    char* base = static_cast<char*>(ws) + kWsHeaderBytes;
     p.ws_o = reinterpret_cast<float*>(base);
     base += slots * p.group * 128 * sizeof(float);
     p.ws_ml = reinterpret_cast<float2*>(base);
 }
 
-
-
 static bool wide_shape(int group, int n_seg) { return group <= 8 && n_seg >= kWideMinSegments; }
+
+// Wide calls merge their split-K pieces inside the decode kernel (each
+// segment has only a few pieces there, so the CTA that completes a segment
+// merges it at little cost); narrow calls have many pieces per segment
+// (batch 1: ~37 at 32k positions) and keep the separate combine kernel,
+// which spreads that merge over one CTA per (segment, q row).
+static bool folded(int group, int n_seg) { return wide_shape(group, n_seg) && n_seg <= kFoldMaxSegments; }
 
 // CTAs of a decode launch (the split-K workspace is sized by it).
 static int decode_grid(int group, int n_seg)
@@ -885,32 +997,48 @@ static int decode_grid(int group, int n_seg)
     return std::min(per_sm * num_sms(), kMaxPieces - 2);
 }
 
+template <int ROWS, int STAGES>
+static size_t decode_smem_bytes()
+{
+    return sizeof(DecodeSmem<ROWS, STAGES>) + 1024;
+}
+
+// Sets the decode kernel's shared-memory attributes on the current device,
+// once per device (again on ordinals past 63).
+template <int ROWS, int STAGES, int CTAS_PER_SM>
+static int ensure_decode_attrs()
+{
+    auto kernel = decode_attention_kernel<ROWS, STAGES, CTAS_PER_SM>;
+    static std::atomic<bool> attr_set[64];
+    int dev = 0;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && attr_set[dev].load(std::memory_order_acquire)) return HX_OK;
+    HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)decode_smem_bytes<ROWS, STAGES>()));
+    HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
+    return HX_OK;
+}
+
 template <int ROWS, int STAGES, int CTAS_PER_SM>
 static int launch_decode(const hx_kv_cache* c, const DecodeParams& p, int n_ctas,
                          cudaStream_t stream)
 {
     auto kernel = decode_attention_kernel<ROWS, STAGES, CTAS_PER_SM>;
-    const size_t smem = sizeof(DecodeSmem<ROWS, STAGES>) + 1024;
-    static std::atomic<bool> attr_set[64];  // per device; set again on ordinals past 63
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-        HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem));
-        HX_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                         (int)cudaSharedmemCarveoutMaxShared));
-        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
-    }
+    const size_t smem = decode_smem_bytes<ROWS, STAGES>();
+    if (int rc = ensure_decode_attrs<ROWS, STAGES, CTAS_PER_SM>()) return rc;
     const bool ov = (c->cfg.flags & HX_KV_OVERLAP_LAUNCH) != 0;
     cudaError_t e = launch_kernel(kernel, dim3(n_ctas), dim3(kDecThreads), smem, stream, ov,
                                   c->tm_k, c->tm_v, p);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention_kernel launch");
     if (int rc = check_launch("decode_attention_kernel")) return rc;
+    if (p.fold_cnt) return HX_OK;  // the decode kernel merged its own pieces
     const int n_items = p.n_seqs * p.view.hkv * p.group;
     // Narrow calls (few segments, many pieces each) take 12 O loads per lane
     // in one round; wide calls have 2-3 pieces per item and keep the 8-load
     // (64-register) variant, which fits beside two decode CTAs per SM.
-    e = launch_kernel(CTAS_PER_SM == 1 ? decode_combine_kernel<12> : decode_combine_kernel<8>,
+    e = launch_kernel(n_ctas <= num_sms() ? decode_combine_kernel<12> : decode_combine_kernel<8>,
                       dim3(n_items), dim3(128), 0, stream, true, p, n_ctas);
     if (e != cudaSuccess) return cuda_fail(e, "decode_combine_kernel launch");
     return check_launch("decode_combine_kernel");
@@ -944,7 +1072,7 @@ static int validate_decode(const hx_kv_cache* c, int layer, const void* q, int q
         return fail(HX_ERR_INVALID, "num_q_heads %d must be a multiple of kv heads %d", num_q_heads, hkv);
     if ((q_dtype != HX_FP16 && q_dtype != HX_FP32) || (out_dtype != HX_FP16 && out_dtype != HX_FP32))
         return fail(HX_ERR_INVALID, "q/out dtype");
-    return HX_OK;
+    return check_device(c->device, "the cache");
 }
 
 // Everything but the output placement (set by the caller afterwards).
@@ -984,7 +1112,10 @@ static int run_decode(const hx_kv_cache* c, DecodeParams& p, void* scratch, cuda
     const int n_seg = p.n_seqs * p.view.hkv;
     const int n_ctas = decode_grid(p.group, n_seg);
     bind_workspace(p, scratch, n_ctas);
-    if (wide_shape(p.group, n_seg)) return launch_decode<8, 3, 2>(c, p, n_ctas, s);
+    if (wide_shape(p.group, n_seg)) {
+        if (folded(p.group, n_seg)) p.fold_cnt = static_cast<unsigned int*>(scratch);
+        return launch_decode<8, 3, 2>(c, p, n_ctas, s);
+    }
     if (p.group <= 8) return launch_decode<8, 6, 1>(c, p, n_ctas, s);
     return launch_decode<16, 6, 1>(c, p, n_ctas, s);
 }
@@ -1091,33 +1222,47 @@ extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const
 // loads the library keeps this array until the process exits.
 //
 // In host code `g_decode_scratch` is only a host-side stand-in for the device
-// array, not a device address; its device address is looked up with
-// cudaGetSymbolAddress once per device, on that device's first call.  That
-// first call on a device should therefore happen before any stream capture.
+// array, not a device address.  Its device address is looked up with
+// cudaGetSymbolAddress once per device by decode_prepare_device, which
+// hx_kv_create and hx_kv_wrap run on the cache's device (where allocating is
+// allowed); that set-up also sets the decode kernels' attributes, loads
+// their module and allocates the device status word, so the entry point
+// itself makes none of these calls.
 //
-// All calls share the array and it keeps the last call's contents: the decode
-// kernel writes every slot its combine step reads within the same call, so
-// nothing needs clearing; but two calls that overlap on the GPU (different
-// streams, devices aside) race on the scratch.  Kernel-side faults of this
-// entry point are not recorded in the device status word (setting that word
-// up may allocate); bounds are still checked and waits still bounded.
+// All calls share the array and it keeps the last call's contents.  Its
+// first 64 KiB are the per-segment counters of the folded combine: zero when
+// the module is loaded, and every call returns them to zero.  Every other
+// word a call reads is written earlier in the same call, so nothing needs
+// clearing; but two calls that overlap on the GPU (different streams,
+// devices aside) race on the scratch.
 namespace hx {
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
-static void* noalloc_scratch_ptr()
+int decode_prepare_device(hx_kv_cache* c)
 {
     static std::mutex mu;
-    static void* ptrs[64] = {nullptr};
+    static void* scratch[64] = {nullptr};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    HX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != c->device) return fail(HX_ERR_INVALID, "cache set-up on device %d, current %d", c->device, dev);
+    if (int rc = ensure_decode_attrs<8, 6, 1>()) return rc;
+    if (int rc = ensure_decode_attrs<8, 3, 2>()) return rc;
+    if (int rc = ensure_decode_attrs<16, 6, 1>()) return rc;
+    cudaFuncAttributes fa;
+    HX_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_combine_kernel<12>));
+    HX_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_combine_kernel<8>));
+    HX_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_generic_kernel));
+    c->status = status_word();
+    if (!c->status) return fail(HX_ERR_CUDA, "device status word allocation failed");
     std::lock_guard<std::mutex> lk(mu);
-    if (!ptrs[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
-        ptrs[dev] = p;
+    void* ptr = dev >= 0 && dev < 64 ? scratch[dev] : nullptr;
+    if (!ptr) {
+        HX_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_decode_scratch));
+        if (dev >= 0 && dev < 64) scratch[dev] = ptr;
     }
-    return ptrs[dev];
+    c->noalloc_scratch = ptr;
+    return HX_OK;
 }
 }  // namespace hx
 
@@ -1139,17 +1284,14 @@ extern "C" int hx_decode_attention_noalloc(const hx_kv_cache* c, int layer, cons
     p.outs[0] = out;
     p.n_outs = 1;
     p.out_vec = reinterpret_cast<uintptr_t>(out) % 16 == 0;
-    p.status = nullptr;
+    p.status = c->status;  // allocated when the cache was created
     const size_t need = needed_scratch(c, p);
     if (need > kNoAllocScratchBytes)
         return fail(HX_ERR_CAPACITY,
                     "this call needs %zu bytes of split-K scratch; the no-allocation entry point "
                     "holds at most %zu (use hx_decode_attention with a caller workspace)",
                     need, kNoAllocScratchBytes);
-    void* scratch = nullptr;
-    if (need) {
-        scratch = noalloc_scratch_ptr();
-        if (!scratch) return fail(HX_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch failed");
-    }
-    return run_decode(c, p, scratch, (cudaStream_t)stream);
+    if (need && !c->noalloc_scratch)
+        return fail(HX_ERR_CUDA, "the decode scratch of this device was not set up");
+    return run_decode(c, p, c->noalloc_scratch, (cudaStream_t)stream);
 }

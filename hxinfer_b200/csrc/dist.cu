@@ -180,6 +180,7 @@ extern "C" int hx_dist_wait(hx_dist* d, uint32_t epoch, hx_stream_t stream)
     HX_NVTX_RANGE("hx_dist_wait");
     if (!d || !d->connected) return fail(HX_ERR_INVALID, "gather endpoint is not connected");
     if (d->world == 1) return HX_OK;
+    if (int rc = check_device(d->device, "the gather endpoint")) return rc;
     PeerFlags peers{};
     for (int r = 0; r < d->world; ++r)
         if (r != d->rank) peers.slot[r] = d->peer_flags[r] + d->rank;

@@ -87,6 +87,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
     }
 }
 
+// GPU-scope acquire-release fence: after a CTA barrier, orders the CTA's
+// earlier global writes before this thread's next atomic (release side), or
+// an atomic's result before the CTA's later reads (acquire side).
+__device__ __forceinline__ void fence_acq_rel_gpu()
+{
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) accesses to the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem()
@@ -191,9 +199,11 @@ inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Physical block of logical block `blk` of sequence `seq`.
+// Physical block of logical block `blk` of sequence `seq`, or -1 when the
+// block is unmapped or (seq, blk) lies outside the block table.
 __device__ __forceinline__ int64_t phys_block(const KVView& v, int seq, int blk)
 {
+    if (seq < 0 || seq >= v.max_seqs || blk < 0 || blk >= v.mbps) return -1;
     if (v.table) return v.table[(int64_t)seq * v.mbps + blk];
     return (int64_t)seq * v.mbps + blk;
 }

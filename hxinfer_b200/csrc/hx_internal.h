@@ -53,6 +53,11 @@ struct hx_kv_cache {
     CUtensorMap tm_k{}, tm_v{};     // 2-D [rows][head_dim] fp16, box 64x64, 128B swizzle
     char* tm_k_base = nullptr;
     char* tm_v_base = nullptr;
+    // Set up at creation on the cache's device (decode_prepare_device): the
+    // device status word and the device address of the no-allocation decode
+    // scratch, so hx_decode_attention_noalloc makes no set-up calls.
+    int* status = nullptr;
+    void* noalloc_scratch = nullptr;
 };
 
 // Peer-to-peer gather of decode outputs across the GPUs of one node: every
@@ -84,10 +89,19 @@ int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
 // Checks the launch that was just issued.
 int check_launch(const char* what);
+// HX_ERR_INVALID unless `device` is the calling thread's current device.
+// Every entry point that launches on a cache, table or endpoint calls it
+// before any launch: a tensor map or block table of one GPU used from a
+// kernel on another would read that GPU's memory as peer memory.
+int check_device(int device, const char* what);
 // Device status word of the current device (allocated on first use).
 int* status_word();
 int num_sms();
 KVView make_view(const hx_kv_cache* c, int layer);
+// Per-device set-up of the decode path for a new cache, on its device:
+// kernel attributes and module loading, the device status word, and the
+// no-allocation scratch address (stored in the cache).
+int decode_prepare_device(hx_kv_cache* c);
 
 }  // namespace hx
 

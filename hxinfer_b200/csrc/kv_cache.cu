@@ -45,6 +45,17 @@ int check_launch(const char* what)
     return HX_OK;
 }
 
+int check_device(int device, const char* what)
+{
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev != device)
+        return fail(HX_ERR_INVALID, "%s lives on device %d but device %d is current", what, device,
+                    dev);
+    return HX_OK;
+}
+
 static std::mutex g_status_mu;
 static int* g_status[64] = {nullptr};
 
@@ -325,6 +336,10 @@ extern "C" int hx_kv_create(const hx_kv_config* cfg, hx_kv_cache** out)
             c->has_tmap = true;
         }
     }
+    if (int rc = decode_prepare_device(c)) {
+        hx_kv_destroy(c);
+        return rc;
+    }
     *out = c;
     return HX_OK;
 }
@@ -368,6 +383,10 @@ extern "C" int hx_kv_wrap(void* k_base, void* v_base, int num_kv_heads, int head
             return rc;
         }
         c->has_tmap = true;
+    }
+    if (int rc = decode_prepare_device(c)) {
+        delete c;
+        return rc;
     }
     *out = c;
     return HX_OK;
@@ -423,6 +442,7 @@ extern "C" int hx_kv_reserve(hx_kv_cache* c, int seq, int n_tokens, hx_stream_t 
         return fail(HX_ERR_CAPACITY, "%d positions exceed the per-sequence capacity %d", n_tokens,
                     c->cfg.max_tokens_per_seq);
     if (c->wrapped) return HX_OK;  // fully mapped by construction
+    if (int rc = check_device(c->device, "the cache")) return rc;
     int need = (n_tokens + kBlockTokens - 1) / kBlockTokens;
     int have = c->n_mapped[seq];
     if (need <= have) return HX_OK;
@@ -442,6 +462,7 @@ extern "C" int hx_kv_release(hx_kv_cache* c, int seq, hx_stream_t stream)
     if (!c) return fail(HX_ERR_INVALID, "null cache");
     if (seq < 0 || seq >= c->cfg.max_seqs) return fail(HX_ERR_INVALID, "seq %d out of range", seq);
     if (c->wrapped) return HX_OK;
+    if (int rc = check_device(c->device, "the cache")) return rc;
     int have = c->n_mapped[seq];
     for (int b = 0; b < have; ++b) {
         int32_t& e = c->h_table[(size_t)seq * c->mbps + b];
@@ -460,7 +481,7 @@ static int check_range(const hx_kv_cache* c, int layer, int seq, int start, int 
     if (start < 0 || n < 0 || (int64_t)start + n > (int64_t)c->n_mapped[seq] * kBlockTokens ||
         (int64_t)start + n > c->cfg.max_tokens_per_seq)
         return fail(HX_ERR_CAPACITY, "positions [%d, %d) not reserved for seq %d", start, start + n, seq);
-    return HX_OK;
+    return check_device(c->device, "the cache");
 }
 
 extern "C" int hx_kv_write(hx_kv_cache* c, int layer, int seq, int start, int n, const void* k,
@@ -498,6 +519,7 @@ extern "C" int hx_kv_read(const hx_kv_cache* c, int layer, int seq, int start, i
 extern "C" int hx_kv_fill_normal(hx_kv_cache* c, uint64_t seed, hx_stream_t stream)
 {
     if (!c) return fail(HX_ERR_INVALID, "null cache");
+    if (int rc = check_device(c->device, "the cache")) return rc;
     auto launch = [&](void* base, size_t bytes, uint64_t s) {
         uint64_t n8 = bytes / 16;
         int blocks = num_sms() * 8;

@@ -459,6 +459,7 @@ extern "C" int hx_prefill_attention(const hx_kv_cache* c, int layer, const void*
     if (reinterpret_cast<uintptr_t>(q) & 15 || reinterpret_cast<uintptr_t>(out) & 15)
         return fail(HX_ERR_INVALID, "q/out must be 16-byte aligned");
     if (n == 0) return HX_OK;
+    if (int rc = check_device(c->device, "the cache")) return rc;
     CUtensorMap tm_q;
     if (int rc = encode_q_map(&tm_q, q, num_q_heads, n)) return rc;
     PrefillParams p{};

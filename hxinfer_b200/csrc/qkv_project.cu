@@ -420,6 +420,9 @@ extern "C" int hx_qkv_rope_append(hx_kv_cache* c, int layer, const void* x, int 
         return fail(HX_ERR_INVALID, "x and the weights must be 16-byte aligned");
     if (table && (table->cfg.head_dim != 128))
         return fail(HX_ERR_INVALID, "rope table head_dim %d != 128", table->cfg.head_dim);
+    if (int rc = check_device(c->device, "the cache")) return rc;
+    if (table)
+        if (int rc = check_device(table->device, "the rope table")) return rc;
     const KVView view = make_view(c, layer);
     cudaStream_t s = (cudaStream_t)stream;
     const int xf = x_dtype == HX_FP32;

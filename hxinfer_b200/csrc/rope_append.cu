@@ -157,6 +157,9 @@ extern "C" int hx_rope_append(hx_kv_cache* c, int layer, const void* q, const vo
     if (q_out && q_out_dtype != HX_FP16 && q_out_dtype != HX_FP32)
         return fail(HX_ERR_INVALID, "q_out dtype %d", q_out_dtype);
     if (n_tokens == 0) return HX_OK;
+    if (int rc = check_device(c->device, "the cache")) return rc;
+    if (table)
+        if (int rc = check_device(table->device, "the rope table")) return rc;
     KVView view = make_view(c, layer);
     const float2* tab = table ? table->d_cos_sin : nullptr;
     const int tmax = table ? table->cfg.max_pos : 0;
@@ -208,6 +211,7 @@ extern "C" int hx_rope_qk(void* q, void* k, int dtype, int rows, int num_q_heads
     if (step < 0 || step >= table->cfg.max_pos)
         return fail(HX_ERR_CAPACITY, "step %d outside the rope table [0, %d)", step, table->cfg.max_pos);
     if (rows == 0) return HX_OK;
+    if (int rc = check_device(table->device, "the rope table")) return rc;
     const float2* cs = table->d_cos_sin + (int64_t)step * (head_dim / 2);
     int64_t items = (int64_t)rows * (num_q_heads + num_kv_heads) * (head_dim / 2);
     int blocks = (int)std::min<int64_t>((items + 255) / 256, 4096);

@@ -155,8 +155,9 @@ static int check_snapshot_args(const hx_kv_cache* c, int seq, int prefix_len, co
         return fail(HX_ERR_INVALID, "snapshot buffer of %zu bytes < %zu needed", bytes,
                     hx_snapshot_bytes(c, prefix_len));
     if (reinterpret_cast<uintptr_t>(buf) & 15) return fail(HX_ERR_INVALID, "snapshot buffer not 16-byte aligned");
-    if (prefix_len > 0) return check_device_accessible(buf);
-    return HX_OK;
+    if (prefix_len == 0) return HX_OK;
+    if (int rc = check_device(c->device, "the cache")) return rc;
+    return check_device_accessible(buf);
 }
 
 extern "C" int hx_kv_snapshot(const hx_kv_cache* c, int seq, int prefix_len, void* dst,

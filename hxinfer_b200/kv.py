@@ -65,6 +65,18 @@ def convert(dst: torch.Tensor, src: torch.Tensor, stream=None):
     check(rc, "hx_convert")
 
 
+def decode_kernel_count(n_segments: int, head_dim: int, group: int) -> int:
+    """Kernels one hx_decode_attention call launches for n_segments
+    (sequence, kv head) pairs, mirroring the library's choice: on the
+    head_dim-128 path (group <= 16) the split-K decode kernel, which merges
+    its own pieces when 64 <= n_segments <= 16384 and group <= 8, and
+    otherwise a combine kernel after it; one generic kernel for other head
+    sizes."""
+    if head_dim == 128 and group <= 16:
+        return 1 if group <= 8 and 64 <= n_segments <= 16384 else 2
+    return 1
+
+
 def prefix_hash(tokens) -> int:
     arr = (C.c_int32 * len(tokens))(*[int(t) for t in tokens])
     return int(load().hx_prefix_hash(arr, len(tokens)))

@@ -203,9 +203,13 @@ int hx_qkv_rope_append(hx_kv_cache* cache, int layer, const void* x, int x_dtype
                        const hx_rope_table* table, void* q_out, int q_out_dtype,
                        hx_stream_t stream);
 
-/* Workspace bytes hx_decode_attention needs for n_seqs sequences (split-K
- * partial results; device memory owned by the caller, no initialisation
- * needed: every value a call reads is written by that call). */
+/* Workspace bytes hx_decode_attention needs for n_seqs sequences: a fixed
+ * 64 KiB block of per-segment arrival counters followed by the split-K
+ * partial results.  Device memory owned by the caller.  Zero-fill it once
+ * before its first use (e.g. cudaMemsetAsync); every call leaves the counters
+ * zero again, so later calls, on any cache and any n_seqs up to the size the
+ * buffer was made for, need no clearing.  Calls that share one workspace must
+ * not overlap on the GPU. */
 size_t hx_decode_workspace_bytes(const hx_kv_cache* cache, int n_seqs, int num_q_heads);
 
 /* K2: split-K GQA decode attention over the cache (replaces
@@ -214,7 +218,9 @@ size_t hx_decode_workspace_bytes(const hx_kv_cache* cache, int n_seqs, int num_q
  * seq_ids, lengths: device int32 [n_seqs] (lengths = positions attended, >= 1);
  * out: device [n_seqs][num_q_heads*head_dim] in out_dtype.
  * q head h reads kv head h / (num_q_heads / num_kv_heads).
- * Two launches: the split-K kernel and its combine kernel. */
+ * One launch when the call has at least 64 (sequence, kv head) pairs and at
+ * most 8 q heads per kv head (the decode kernel merges its own split-K
+ * pieces); otherwise the split-K kernel and its combine kernel. */
 int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
                         const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
                         int num_q_heads, float scale, void* out, int out_dtype, void* workspace,
@@ -239,10 +245,14 @@ int hx_prefill_attention(const hx_kv_cache* cache, int layer, const void* q, int
  * other allocating call.  No counterpart exists in the reference engine.
  * Its split-K scratch is a fixed 4 MiB array inside the library, which every
  * GPU that loads the library keeps until exit; calls needing more
- * (hx_decode_workspace_bytes > 4 MiB) fail with HX_ERR_CAPACITY.  The first
- * call on each device looks up the array's device address, so make it before
- * any stream capture.  All calls share the array: calls that overlap on the
- * GPU race.  Kernel-side faults are not recorded in the device status word. */
+ * (hx_decode_workspace_bytes > 4 MiB) fail with HX_ERR_CAPACITY.  The array's
+ * device address, the kernels' attributes and the device status word are
+ * set up once per device by hx_kv_create / hx_kv_wrap, on the cache's device,
+ * where allocating is allowed; this entry point itself makes no set-up call.
+ * All calls share the array and it keeps the last call's contents (its
+ * counters are back at zero after every call): calls that overlap on the GPU
+ * race.  Kernel-side faults are recorded in the device status word as for
+ * hx_decode_attention. */
 int hx_decode_attention_noalloc(const hx_kv_cache* cache, int layer, const void* q, int q_dtype,
                                 const int32_t* seq_ids, const int32_t* lengths, int n_seqs,
                                 int num_q_heads, float scale, void* out, int out_dtype,

@@ -211,8 +211,8 @@ def test_decode_batched_llama3(hx, oracle):
 
 
 def test_decode_repeated_calls_share_workspace(hx, oracle):
-    """Split-K pieces meet through generation-tagged tickets in the workspace:
-    repeated calls on one workspace (no clearing) give identical outputs."""
+    """The split-K pieces of a call meet in the workspace: repeated calls on
+    one workspace (no clearing in between) give identical outputs."""
     rng = np.random.default_rng(60)
     Hq, Hkv, lengths = 28, 4, [32769, 1025, 70]
     cache = make_cache(hx, 1, Hkv, 3, 32769)
@@ -258,20 +258,28 @@ def test_decode_unaligned_out_matches_aligned(hx, out_dtype):
     assert buf[0].item() == 0
 
 
-def test_decode_cuda_graph_replays(hx, oracle):
-    """A captured append+decode step replays correctly many times on one
-    workspace (the per-segment tickets reset themselves)."""
+@pytest.mark.parametrize("wide", [False, True])
+def test_decode_cuda_graph_replays(hx, oracle, wide):
+    """A captured decode replays correctly many times on one workspace.  The
+    wide case (128 (sequence, kv head) segments) merges its split-K pieces
+    inside the decode kernel through per-segment counters, which every call
+    returns to zero."""
     rng = np.random.default_rng(64)
-    Hq, Hkv, lengths = 28, 4, [32769, 700]
-    cache = make_cache(hx, 1, Hkv, 2, 32770)
+    if wide:
+        Hq, Hkv = 32, 8
+        lengths = [int(x) for x in rng.integers(1, 3000, 16)]
+    else:
+        Hq, Hkv, lengths = 28, 4, [32769, 700]
+    n = len(lengths)
+    cache = make_cache(hx, 1, Hkv, n, max(lengths) + 1)
     for s, L in enumerate(lengths):
         cache.reserve(s, L)
     cache.fill_normal(65)
-    q = torch.from_numpy(rng.standard_normal((2, Hq * 128)).astype(np.float16)).cuda()
-    sid = torch.arange(2, dtype=torch.int32, device="cuda")
+    q = torch.from_numpy(rng.standard_normal((n, Hq * 128)).astype(np.float16)).cuda()
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
     lens = dev(np.array(lengths, np.int32))
-    ws = torch.zeros(cache.workspace_bytes(2, Hq), dtype=torch.uint8, device="cuda")
-    out = torch.empty((2, Hq * 128), dtype=torch.float16, device="cuda")
+    ws = torch.zeros(cache.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda")
+    out = torch.empty((n, Hq * 128), dtype=torch.float16, device="cuda")
     cache.decode(0, q, sid, lens, Hq, out=out, workspace=ws)  # eager first
     torch.cuda.synchronize()
     want = out.clone()
@@ -286,13 +294,58 @@ def test_decode_cuda_graph_replays(hx, oracle):
         torch.cuda.synchronize()
         assert torch.equal(out.view(torch.int16), want.view(torch.int16))
     hx.device_status()
+    got = want.float().cpu().numpy()
+    for s in (0, n - 1):
+        k, v = cache.read(0, s, 0, lengths[s])
+        ref = oracle.decode_attention(q[s].float().cpu().numpy(),
+                                      k.reshape(lengths[s], -1).float().cpu().numpy(),
+                                      v.reshape(lengths[s], -1).float().cpu().numpy(), Hq, Hkv, 128)
+        assert_close(got[s], ref, f"seq {s} after graph replays")
 
 
-def _decode_steps(hx, overlap, graph, layers=4, steps=3):
+def test_decode_folded_workspace_reuse_across_batches(hx, oracle):
+    """One workspace serves, in turn, a wide call that merges inside the decode
+    kernel (64 sequences x 8 kv heads), a narrow call with the combine kernel
+    (4 sequences) and the wide call again: the per-segment counters are back
+    at zero after every call, so the third call equals the first bit for bit
+    and matches the oracle."""
+    rng = np.random.default_rng(70)
+    Hq, Hkv = 32, 8
+    lengths = [int(x) for x in rng.integers(1, 2500, 64)]
+    n = len(lengths)
+    cache = make_cache(hx, 1, Hkv, n, max(lengths))
+    for s, L in enumerate(lengths):
+        cache.reserve(s, L)
+    cache.fill_normal(71)
+    q = torch.from_numpy(rng.standard_normal((n, Hq * 128)).astype(np.float16)).cuda()
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
+    lens = dev(np.array(lengths, np.int32))
+    ws = torch.zeros(cache.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda")
+    first = cache.decode(0, q, sid, lens, Hq, workspace=ws)
+    narrow = cache.decode(0, q[:4].contiguous(), sid[:4].contiguous(), lens[:4].contiguous(), Hq,
+                          workspace=ws)
+    again = cache.decode(0, q, sid, lens, Hq, workspace=ws)
+    torch.cuda.synchronize()
+    hx.device_status()
+    assert torch.equal(first.view(torch.int16), again.view(torch.int16))
+    assert torch.equal(first[:4].view(torch.int16), narrow.view(torch.int16)) or \
+        np.allclose(first[:4].float().cpu().numpy(), narrow.float().cpu().numpy(), atol=ATOL, rtol=RTOL)
+    got = again.float().cpu().numpy()
+    for s in range(0, n, 9):
+        k, v = cache.read(0, s, 0, lengths[s])
+        ref = oracle.decode_attention(q[s].float().cpu().numpy(),
+                                      k.reshape(lengths[s], -1).float().cpu().numpy(),
+                                      v.reshape(lengths[s], -1).float().cpu().numpy(), Hq, Hkv, 128)
+        assert_close(got[s], ref, f"seq {s} L={lengths[s]}")
+
+
+def _decode_steps(hx, overlap, graph, layers=4, steps=3, wide=False):
     """rope_append -> decode over `layers` layers for `steps` steps; returns
     every step's outputs."""
     Hq, Hkv, hd = 28, 4, 128
     lengths = np.array([5000, 130, 64], np.int32)
+    if wide:  # 20 sequences x 4 kv heads: the decode kernel merges its own pieces
+        lengths = np.random.default_rng(98).integers(1, 5000, 20).astype(np.int32)
     n = len(lengths)
     cache = hx.KVCache(layers, Hkv, hd, n, 5100, overlap=overlap)
     for s_, L in enumerate(lengths):
@@ -340,12 +393,13 @@ def _decode_steps(hx, overlap, graph, layers=4, steps=3):
 
 
 @pytest.mark.parametrize("graph", [False, True])
-def test_decode_overlap_launch_matches(hx, graph):
+@pytest.mark.parametrize("wide", [False, True])
+def test_decode_overlap_launch_matches(hx, graph, wide):
     """HX_KV_OVERLAP_LAUNCH (programmatic dependent launch of the
     append -> decode chain) changes timing only: outputs equal the serialised
     launches bit for bit."""
-    a = _decode_steps(hx, overlap=False, graph=graph)
-    b = _decode_steps(hx, overlap=True, graph=graph)
+    a = _decode_steps(hx, overlap=False, graph=graph, wide=wide)
+    b = _decode_steps(hx, overlap=True, graph=graph, wide=wide)
     for x, y in zip(a, b):
         assert torch.equal(x.view(torch.int16), y.view(torch.int16))
 
