@@ -109,6 +109,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy()
     return policy;
 }
 
+__device__ __forceinline__ uint64_t l2_evict_last_policy()
+{
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
 // 2-D TMA tile load global -> shared, completing on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tm, int x, int y,
                                             uint64_t* bar, uint64_t policy)

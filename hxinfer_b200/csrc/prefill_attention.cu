@@ -29,6 +29,7 @@ namespace hx {
 
 constexpr int kPfThreads = 192;
 constexpr int kRegionBytes = 128 * 128;  // 128 rows x 64 fp16 (one 128-byte swizzled region)
+constexpr int kPfKStages = 3, kPfVStages = 3;  // K and V tile rings
 
 struct PrefillParams {
     KVView view;
@@ -40,14 +41,14 @@ struct PrefillParams {
 };
 
 struct PrefillSmem {
-    uint8_t q[2][kRegionBytes];        // [d half]
-    uint8_t k[2][2][kRegionBytes];     // [stage][d half]
-    uint8_t v[2][2][kRegionBytes];     // [stage][d half]
-    uint8_t p[2][kRegionBytes];        // [key half]
+    uint8_t q[2][kRegionBytes];                // [d half]
+    uint8_t k[kPfKStages][2][kRegionBytes];    // [stage][d half]
+    uint8_t v[kPfVStages][2][kRegionBytes];    // [stage][d half]
     uint64_t q_full;
-    uint64_t kv_full[2], kv_empty[2];
-    uint64_t s_full[2], s_free[2];
-    uint64_t p_full, pv_done, mma_idle;
+    uint64_t k_full[kPfKStages], k_empty[kPfKStages];
+    uint64_t v_full[kPfVStages], v_empty[kPfVStages];
+    uint64_t s_full[2], p_full[2], pv_done[2];  // per TMEM S/P buffer
+    uint64_t mma_idle;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -77,6 +78,19 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The same MMA with the A operand (M = 128 rows x K = 16 fp16) read from
+// tensor memory: row i in lane i, two K elements per 32-bit column.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -128,6 +142,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v)
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v)
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -169,14 +197,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(&sm.q_full, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&sm.kv_full[i], 1);
-            mbar_init(&sm.kv_empty[i], 1);
-            mbar_init(&sm.s_full[i], 1);
-            mbar_init(&sm.s_free[i], 4);
+        for (int i = 0; i < kPfKStages; ++i) {
+            mbar_init(&sm.k_full[i], 1);
+            mbar_init(&sm.k_empty[i], 1);
         }
-        mbar_init(&sm.p_full, 4);
-        mbar_init(&sm.pv_done, 1);
+        for (int i = 0; i < kPfVStages; ++i) {
+            mbar_init(&sm.v_full[i], 1);
+            mbar_init(&sm.v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.s_full[i], 1);
+            mbar_init(&sm.p_full[i], 4);
+            mbar_init(&sm.pv_done[i], 1);
+        }
         mbar_init(&sm.mma_idle, 1);
         sm.abort_flag = 0;
         fence_mbar_init();
@@ -193,83 +226,112 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t tmem = sm.tmem_base;
 
     if (warp == 4) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            const uint64_t pol = l2_evict_first_policy();
-            mbar_arrive_expect_tx(&sm.q_full, 2 * kRegionBytes);
-            tma_load_2d(sm.q[0], &tm_q, h * 128, q0, &sm.q_full, pol);
-            tma_load_2d(sm.q[1], &tm_q, h * 128 + 64, q0, &sm.q_full, pol);
+        // ------------------------------------------------------------ TMA producers
+        // lane 0: Q, then the K ring; lane 1: the V ring (V tiles are needed
+        // one softmax later than K tiles, so each ring runs at its own pace)
+        if (lane < 2) {
+            // Q is read by this CTA only; a head's K/V tiles are read again by
+            // every later query tile of the head (and by the other q heads of
+            // its group), so they are kept in L2
+            const uint64_t pol = l2_evict_last_policy();
             const KVView& v = p.view;
+            const bool is_k = lane == 0;
+            const int stages = is_k ? kPfKStages : kPfVStages;
+            if (is_k) {
+                const uint64_t qpol = l2_evict_first_policy();
+                mbar_arrive_expect_tx(&sm.q_full, 2 * kRegionBytes);
+                tma_load_2d(sm.q[0], &tm_q, h * 128, q0, &sm.q_full, qpol);
+                tma_load_2d(sm.q[1], &tm_q, h * 128 + 64, q0, &sm.q_full, qpol);
+            }
             int issued = 0;
+            // Block-table entries of tile j + 1 are read while tile j's ring
+            // slot is awaited, so no table load sits between a freed slot and
+            // its copy.  -2 marks a block past the keys this tile needs.
+            auto table_pair = [&](int j, int64_t* pb) {
+                for (int b = 0; b < 2; ++b) {
+                    const int blk = 2 * j + b;
+                    pb[b] = blk * kBlockTokens < kend ? phys_block(v, p.seq, blk) : -2;
+                }
+            };
+            int64_t next_pb[2];
+            table_pair(0, next_pb);
             for (int j = 0; j < nk; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !pf_wait(sm, &sm.kv_empty[s], ((j >> 1) - 1) & 1, p.status)) break;
+                const int s = j % stages;
+                uint64_t* full = is_k ? &sm.k_full[s] : &sm.v_full[s];
+                uint64_t* empty = is_k ? &sm.k_empty[s] : &sm.v_empty[s];
+                const int64_t pb[2] = {next_pb[0], next_pb[1]};
+                if (j + 1 < nk) table_pair(j + 1, next_pb);
+                if (j >= stages && !pf_wait(sm, empty, ((j / stages) - 1) & 1, p.status)) break;
                 int64_t rows[2];
                 uint32_t bytes = 0;
                 for (int b = 0; b < 2; ++b) {
-                    const int blk = 2 * j + b;
                     rows[b] = -1;
-                    if (blk * kBlockTokens >= kend) continue;
-                    const int64_t pb = phys_block(v, p.seq, blk);
-                    if (pb < 0) {
+                    if (pb[b] == -2) continue;
+                    if (pb[b] < 0) {
                         record_status(p.status, HX_ERR_CAPACITY);
                         continue;
                     }
-                    rows[b] = (pb * v.block_stride + (int64_t)kvh * v.head_stride) / 256;
-                    bytes += 4 * (kRegionBytes / 2);
+                    rows[b] = (pb[b] * v.block_stride + (int64_t)kvh * v.head_stride) / 256;
+                    bytes += 2 * (kRegionBytes / 2);
                 }
-                mbar_arrive_expect_tx(&sm.kv_full[s], bytes);
+                mbar_arrive_expect_tx(full, bytes);
+                uint8_t(*dst)[kRegionBytes] = is_k ? sm.k[s] : sm.v[s];
+                const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+                const int64_t row0 = is_k ? v.k_row0 : v.v_row0;
                 for (int b = 0; b < 2; ++b) {
                     if (rows[b] < 0) continue;
-                    const int rk = (int)(v.k_row0 + rows[b]), rv = (int)(v.v_row0 + rows[b]);
+                    const int r = (int)(row0 + rows[b]);
                     const int off = b * (kRegionBytes / 2);
-                    tma_load_2d(sm.k[s][0] + off, &tm_k, 0, rk, &sm.kv_full[s], pol);
-                    tma_load_2d(sm.k[s][1] + off, &tm_k, 64, rk, &sm.kv_full[s], pol);
-                    tma_load_2d(sm.v[s][0] + off, &tm_v, 0, rv, &sm.kv_full[s], pol);
-                    tma_load_2d(sm.v[s][1] + off, &tm_v, 64, rv, &sm.kv_full[s], pol);
+                    tma_load_2d(dst[0] + off, tm, 0, r, full, pol);
+                    tma_load_2d(dst[1] + off, tm, 64, r, full, pol);
                 }
                 issued = j + 1;
             }
             // Copies still in flight must land before the CTA exits (bounded).
-            mbar_wait(&sm.q_full, 0);
-            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1);
+            if (is_k) mbar_wait(&sm.q_full, 0);
+            for (int j = issued > stages ? issued - stages : 0; j < issued; ++j)
+                mbar_wait(is_k ? &sm.k_full[j % stages] : &sm.v_full[j % stages], (j / stages) & 1);
         }
     } else if (warp == 5) {
         // ------------------------------------------------------------ MMA issuer
+        // Order: S_0, S_1, then for each j: PV_j, S_{j+2}.  S_j lands in TMEM
+        // buffer j & 1 (columns 128 (j & 1) ..); the softmax writes P_j over
+        // it as fp16 and PV_j reads it from there, so S_{j+2} (same buffer)
+        // is issued after PV_j, and this thread's MMAs execute in order.
         if (lane == 0) {
             const uint32_t id_qk = umma_idesc(false), id_pv = umma_idesc(true);
             bool ok = pf_wait(sm, &sm.q_full, 0, p.status);
-            for (int j = 0; ok && j <= nk; ++j) {
-                if (j < nk) {
-                    const int s = j & 1, b = j & 1;
-                    ok = pf_wait(sm, &sm.kv_full[s], (j >> 1) & 1, p.status);
-                    if (ok && j >= 2) ok = pf_wait(sm, &sm.s_free[b], ((j >> 1) - 1) & 1, p.status);
-                    if (!ok) break;
-                    tc_fence_after();
+            auto issue_s = [&](int j) {
+                const int ks = j % kPfKStages;
+                if (!pf_wait(sm, &sm.k_full[ks], (j / kPfKStages) & 1, p.status)) return false;
+                tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t a = umma_desc(smem_u32(sm.q[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = umma_desc(smem_u32(sm.k[s][kk >> 2]) + (kk & 3) * 32, 16, 1024);
-                        umma_f16(tmem + 128 * b, a, bd, id_qk, kk > 0);
-                    }
-                    umma_commit(&sm.s_full[b]);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t a = umma_desc(smem_u32(sm.q[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = umma_desc(smem_u32(sm.k[ks][kk >> 2]) + (kk & 3) * 32, 16, 1024);
+                    umma_f16(tmem + 128 * (j & 1), a, bd, id_qk, kk > 0);
                 }
-                if (j >= 1) {
-                    const int jj = j - 1, sp = jj & 1;
-                    if (!pf_wait(sm, &sm.p_full, jj & 1, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                umma_commit(&sm.s_full[j & 1]);
+                umma_commit(&sm.k_empty[ks]);
+                return true;
+            };
+            if (ok && nk > 0) ok = issue_s(0);
+            if (ok && nk > 1) ok = issue_s(1);
+            for (int j = 0; ok && j < nk; ++j) {
+                const int vs = j % kPfVStages;
+                if (!pf_wait(sm, &sm.p_full[j & 1], (j >> 1) & 1, p.status) ||
+                    !pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status))
+                    break;
+                tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t a = umma_desc(smem_u32(sm.p[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = umma_desc(smem_u32(sm.v[sp][0]) + kk * 2048, kRegionBytes, 1024);
-                        umma_f16(tmem + 256, a, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    umma_commit(&sm.kv_empty[sp]);
-                    umma_commit(&sm.pv_done);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t bd = umma_desc(smem_u32(sm.v[vs][0]) + kk * 2048, kRegionBytes, 1024);
+                    umma_f16_ts(tmem + 256, tmem + 128 * (j & 1) + 8 * kk, bd, id_pv,
+                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
+                umma_commit(&sm.pv_done[j & 1]);
+                umma_commit(&sm.v_empty[vs]);
+                if (j + 2 < nk) ok = issue_s(j + 2);
             }
             // Every MMA this thread issued must finish before TMEM is freed.
             umma_commit(&sm.mma_idle);
@@ -280,10 +342,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int t = threadIdx.x;  // query row within the tile
         const int row_pos = p.start + q0 + t;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        float m_run = -INFINITY, l = 0.f;
+        const float sc = p.scale_log2;
+        float m_run = -INFINITY, l = 0.f;  // running max (scaled, log2 domain) and sum
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
-            const int b = j & 1, s = j & 1;
+            const int b = j & 1;
             if (!pf_wait(sm, &sm.s_full[b], (j >> 1) & 1, p.status)) {
                 ok = false;
                 break;
@@ -293,28 +356,34 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + 128 * b + 32 * c, sv + 32 * c);
             tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.s_free[b]);
             const int k0 = 128 * j;
-            float mt = -INFINITY;
+            const int lim = row_pos - k0;  // keys c <= lim are visible to this row
+            if (lim < 127) {
 #pragma unroll
-            for (int c = 0; c < 128; ++c) {
-                const float x = (k0 + c <= row_pos) ? sv[c] * p.scale_log2 : -INFINITY;
-                sv[c] = x;
-                mt = fmaxf(mt, x);
+                for (int c = 0; c < 128; ++c) sv[c] = c <= lim ? sv[c] : -INFINITY;
             }
-            if (j >= 1) {
-                // P_{j-1} V_{j-1} finished: the P buffer is free and O is stable
-                if (!pf_wait(sm, &sm.pv_done, (j - 1) & 1, p.status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-            }
+            // row max as a tree of eight independent chains
+            float mx8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
+#pragma unroll
+            for (int c = 8; c < 128; c += 8)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], sv[c + e]);
+#pragma unroll
+            for (int w = 4; w; w >>= 1)
+#pragma unroll
+                for (int e = 0; e < w; ++e) mx8[e] = fmaxf(mx8[e], mx8[e + w]);
+            const float mt = mx8[0] * sc;  // the scale is positive: the max commutes with it
             if (mt > m_run + 8.f) {
                 const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
                 if (j >= 1 && alpha < 1.f) {
+                    // O must be stable: P_{j-1} V_{j-1} has finished
+                    if (!pf_wait(sm, &sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
                     const uint32_t oaddr = lane_base + 256;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -330,10 +399,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 l *= alpha;
                 m_run = mt;
             }
+            // P_j = 2^(s * scale - m) as fp16 pairs over S_j's own columns:
+            // column c of this lane holds keys 2c (low half) and 2c + 1
+            const float nm = -m_run;
+            uint32_t pw[64];
+            float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight partial sums
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const float p0 = fast_exp2(fmaf(sv[2 * c], sc, nm));
+                const float p1 = fast_exp2(fmaf(sv[2 * c + 1], sc, nm));
+                l8[c & 7] += p0 + p1;
+                pw[c] = pack_half2(p0, p1);
+            }
+            l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+            tmem_st32u(lane_base + 128 * b, pw);
+            tmem_st32u(lane_base + 128 * b + 32, pw + 32);
+            tmem_st_wait();
             if (k0 + 128 > kend) {
                 // V rows past the last needed key may hold stale bytes: zero
                 // this thread's row so 0 * garbage cannot reach O.
-                if (!pf_wait(sm, &sm.kv_full[s], (j >> 1) & 1, p.status)) {
+                const int vs = j % kPfVStages;
+                if (!pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status)) {
                     ok = false;
                     break;
                 }
@@ -342,57 +428,54 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     for (int dh = 0; dh < 2; ++dh)
 #pragma unroll
                         for (int ch = 0; ch < 8; ++ch)
-                            *reinterpret_cast<uint4*>(sm.v[s][dh] + t * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                            *reinterpret_cast<uint4*>(sm.v[vs][dh] + t * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
                 }
+                fence_proxy_async_smem();
             }
-            // P row t: keys c = 64*kh + 8*ch + e at region kh, 16-byte chunk ch ^ (t & 7)
-#pragma unroll
-            for (int kh = 0; kh < 2; ++kh) {
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = 64 * kh + 8 * ch + 2 * e;
-                        const float p0 = fast_exp2(sv[c] - m_run), p1 = fast_exp2(sv[c + 1] - m_run);
-                        l += p0 + p1;
-                        w[e] = pack_half2(p0, p1);
-                    }
-                    *reinterpret_cast<uint4*>(sm.p[kh] + t * 128 + ((ch ^ (t & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-            fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.p_full);
+            if (lane == 0) mbar_arrive(&sm.p_full[b]);
         }
-        if (ok && pf_wait(sm, &sm.pv_done, (nk - 1) & 1, p.status)) {
+        const bool have_o =
+            ok && nk > 0 && pf_wait(sm, &sm.pv_done[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status);
+        // Epilogue: O / l goes through shared memory (the K ring is idle once
+        // the last PV has completed: every S MMA completed before it) so the
+        // global stores are coalesced.  Row t is staged at t * row_bytes with
+        // its 16-byte chunks permuted (chunk ^ (t & mask)) to spread banks.
+        const int row_bytes = p.out_f32 ? 512 : 256;
+        const int chunks = row_bytes / 16, cmask = chunks - 1;
+        uint8_t* stage = &sm.k[0][0][0];
+        if (have_o) {
             tc_fence_after();
             const float inv = 1.f / l;
-            const bool valid = t < rows_valid;
-            const int64_t obase = ((int64_t)(q0 + t) * p.hq + h) * 128;
+            uint8_t* srow = stage + t * row_bytes;
+            float ov[128];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float ov[32];
-                tmem_ld32(lane_base + 256 + 32 * c, ov);
-                tmem_ld_wait();
-                if (!valid) continue;
-                if (p.out_f32) {
-                    float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + 32 * c);
+            for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + 256 + 32 * c, ov + 32 * c);
+            tmem_ld_wait();
+            if (p.out_f32) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        o4[e] = make_float4(ov[4 * e] * inv, ov[4 * e + 1] * inv, ov[4 * e + 2] * inv,
-                                            ov[4 * e + 3] * inv);
-                } else {
-                    uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + obase + 32 * c);
+                for (int e = 0; e < 32; ++e)
+                    *reinterpret_cast<float4*>(srow + 16 * (e ^ (t & cmask))) =
+                        make_float4(ov[4 * e] * inv, ov[4 * e + 1] * inv, ov[4 * e + 2] * inv,
+                                    ov[4 * e + 3] * inv);
+            } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        o4[e] = make_uint4(pack_half2(ov[8 * e] * inv, ov[8 * e + 1] * inv),
-                                           pack_half2(ov[8 * e + 2] * inv, ov[8 * e + 3] * inv),
-                                           pack_half2(ov[8 * e + 4] * inv, ov[8 * e + 5] * inv),
-                                           pack_half2(ov[8 * e + 6] * inv, ov[8 * e + 7] * inv));
-                }
+                for (int e = 0; e < 16; ++e)
+                    *reinterpret_cast<uint4*>(srow + 16 * (e ^ (t & cmask))) =
+                        make_uint4(pack_half2(ov[8 * e] * inv, ov[8 * e + 1] * inv),
+                                   pack_half2(ov[8 * e + 2] * inv, ov[8 * e + 3] * inv),
+                                   pack_half2(ov[8 * e + 4] * inv, ov[8 * e + 5] * inv),
+                                   pack_half2(ov[8 * e + 6] * inv, ov[8 * e + 7] * inv));
+            }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+        if (have_o) {
+            uint8_t* out = static_cast<uint8_t*>(p.out);
+            for (int u = t; u < rows_valid * chunks; u += 128) {
+                const int r = u / chunks, ch = u % chunks;
+                const uint4 val = *reinterpret_cast<const uint4*>(stage + r * row_bytes + 16 * (ch ^ (r & cmask)));
+                *reinterpret_cast<uint4*>(out + ((int64_t)(q0 + r) * p.hq + h) * row_bytes + 16 * ch) = val;
             }
         }
     }

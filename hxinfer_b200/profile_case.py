@@ -5,6 +5,7 @@
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
+    python -m hxinfer_b200.profile_case c5 --len 2048 --new 256 --steps 128 --layers 28 --conts 32
     python -m hxinfer_b200.profile_case qkv --shape qwen --seqs 1 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case convert --mib 1024 --iters 10
 
@@ -222,6 +223,126 @@ def c2_case(a):
                       "decode_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9}))
 
 
+def c5_case(a):
+    """Prefix-cache reuse on the Qwen2.5-7B attention shape (28 layers, 28 q /
+    4 kv heads, theta 1e6), attention-layer level (q/k/v are synthetic; the
+    projections and the rest of the model are not run).  A `prefix`-token
+    prompt is appended (K1) and prefilled (K3) once on sequence 0 and
+    snapshotted (K4).  Each of `conts` continuations then restores the
+    snapshot into sequence 1, appends and prefills `new` tokens at positions
+    prefix .. prefix+new-1, and decodes `steps` tokens (K1 + K2 per layer, one
+    CUDA graph).  The alternative recomputes: sequence 2 appends and prefills
+    all prefix+new tokens from position 0, then decodes the same steps."""
+    hq, hkv, theta = 28, 4, 1e6
+    hd, layers, P, NP, ND, NC = 128, a.layers, a.len, a.new, a.steps, a.conts
+    cap = P + NP + ND
+    dev = torch.device("cuda")
+    cache = kv.KVCache(layers, hkv, hd, 3, cap)
+    for s in range(3):
+        cache.reserve(s, cap)
+    table = kv.RopeTable(hd, cap, theta)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+
+    def rnd(*shape):
+        return torch.randn(shape, generator=g, device=dev).half()
+
+    qp, kp, vp = rnd(P + NP, hq * hd), rnd(P + NP, hkv * hd), rnd(P + NP, hkv * hd)
+    qd, kd, vd = rnd(ND, 1, hq * hd), rnd(ND, 1, hkv * hd), rnd(ND, 1, hkv * hd)
+    q_rot = torch.empty_like(qp)
+    out_p = torch.empty_like(qp)
+    qd_rot = torch.empty_like(qd)
+    out_d = torch.empty_like(qd)
+    ws = torch.zeros(cache.workspace_bytes(1, hq), dtype=torch.uint8, device=dev)
+    snap = torch.empty(cache.snapshot_bytes(P), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream()
+    sid = {s: torch.full((P + NP,), s, dtype=torch.int32, device=dev) for s in range(3)}
+    pos_all = torch.arange(P + NP, dtype=torch.int32, device=dev)
+
+    def prefill(seq, start, n):
+        sl = slice(start, start + n)
+        for l in range(layers):
+            cache.rope_append(l, kp[sl], vp[sl], sid[seq][:n], pos_all[sl], q=qp[sl], num_q_heads=hq,
+                              table=table, q_out=q_rot[sl], stream=stream)
+            cache.prefill(l, q_rot[sl], seq, start, hq, out=out_p[sl], stream=stream)
+
+    dpos = torch.arange(P + NP, cap, dtype=torch.int32, device=dev).view(ND, 1)
+    dlen = dpos + 1
+
+    def decode(seq):
+        s1 = sid[seq][:1]
+        for t in range(ND):
+            for l in range(layers):
+                cache.rope_append(l, kd[t], vd[t], s1, dpos[t], q=qd[t], num_q_heads=hq,
+                                  table=table, q_out=qd_rot[t], stream=stream)
+                cache.decode(l, qd_rot[t], s1, dlen[t], hq, out=out_d[t], workspace=ws,
+                             stream=stream)
+
+    def ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+    with torch.cuda.stream(stream):
+        prefill(0, 0, P)
+        cache.snapshot(0, P, snap, stream=stream)
+        cache.restore(1, P, snap, stream=stream)
+        prefill(1, P, NP)
+        prefill(2, 0, P + NP)
+        decode(1)  # warm-up outside capture
+        torch.cuda.synchronize()
+        graphs = {}
+        for seq in (1, 2):
+            graphs[seq] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphs[seq], stream=stream):
+                decode(seq)
+        # prefix once, then snapshot
+        e = [ev()]
+        prefill(0, 0, P)
+        e.append(ev())
+        cache.snapshot(0, P, snap, stream=stream)
+        e.append(ev())
+        t_restore, t_new, t_dec, t_recompute, t_dec2 = [], [], [], [], []
+        for _ in range(NC):
+            c = [ev()]
+            cache.restore(1, P, snap, stream=stream)
+            c.append(ev())
+            prefill(1, P, NP)
+            c.append(ev())
+            graphs[1].replay()
+            c.append(ev())
+            prefill(2, 0, P + NP)
+            c.append(ev())
+            graphs[2].replay()
+            c.append(ev())
+            torch.cuda.synchronize()
+            t_restore.append(c[0].elapsed_time(c[1]))
+            t_new.append(c[1].elapsed_time(c[2]))
+            t_dec.append(c[2].elapsed_time(c[3]))
+            t_recompute.append(c[3].elapsed_time(c[4]))
+            t_dec2.append(c[4].elapsed_time(c[5]))
+        torch.cuda.synchronize()
+    kv.device_status()
+    med = lambda x: sorted(x)[len(x) // 2]  # noqa: E731
+    payload = cache.snapshot_bytes(P)
+    reuse_ms = med(t_restore) + med(t_new) + med(t_dec)
+    recompute_ms = med(t_recompute) + med(t_dec2)
+    toks = NP + ND
+    print(json.dumps({
+        "case": "c5", "shape": "qwen", "layers": layers, "prefix": P, "new": NP, "decode_steps": ND,
+        "continuations": NC, "payload_bytes": payload,
+        "prefix_prefill_ms": e[0].elapsed_time(e[1]), "snapshot_ms": e[1].elapsed_time(e[2]),
+        "snapshot_payload_gbs": payload / (e[1].elapsed_time(e[2]) * 1e-3) / 1e9,
+        "restore_ms": med(t_restore), "restore_payload_gbs": payload / (med(t_restore) * 1e-3) / 1e9,
+        "new_prefill_ms": med(t_new), "decode_ms": med(t_dec),
+        "reuse_ms_per_continuation": reuse_ms,
+        "recompute_prefill_ms": med(t_recompute), "recompute_ms_per_continuation": recompute_ms,
+        "reuse_tok_s": toks / (reuse_ms * 1e-3), "recompute_tok_s": toks / (recompute_ms * 1e-3),
+        "speedup": recompute_ms / reuse_ms}))
+    cache.close()
+    table.close()
+
+
 def qkv_case(a):
     """Decode-step QKV projection of one layer for `seqs` tokens: the fused
     hx_qkv_rope_append against the unfused chain (three cuBLAS GEMMs through
@@ -315,7 +436,7 @@ def convert_case(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "qkv", "convert"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "c5", "qkv", "convert"])
     ap.add_argument("--mib", type=int, default=1024, help="convert: MiB of source data")
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
@@ -323,13 +444,15 @@ def main():
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--start", type=int, default=0)
-    ap.add_argument("--steps", type=int, default=1024, help="c2: decode steps after the prompt")
+    ap.add_argument("--steps", type=int, default=1024, help="c2, c5: decode steps after the prompt")
+    ap.add_argument("--new", type=int, default=256, help="c5: tokens prefilled after the restored prefix")
+    ap.add_argument("--conts", type=int, default=32, help="c5: continuations of the prefix")
     ap.add_argument("--overlap", action="store_true",
                     help="programmatic dependent launch of append -> decode (HX_KV_OVERLAP_LAUNCH)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case,
-     "c2": c2_case, "qkv": qkv_case, "convert": convert_case}[a.case](a)
+     "c2": c2_case, "c5": c5_case, "qkv": qkv_case, "convert": convert_case}[a.case](a)
 
 
 if __name__ == "__main__":

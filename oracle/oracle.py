@@ -86,6 +86,8 @@ def ref():
             raise RuntimeError(f"reference library missing: {path} (run make -C oracle ref)")
         R = C.CDLL(path)
         R.ref_rope_cpu.argtypes = [_F, _F, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]
+        R.ref_rope_cuda.argtypes = [_F, _F, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                    C.c_int, C.c_float, C.c_float, C.c_float, C.c_int]
         R.ref_softmax_cpu.argtypes = [_F, _F, C.c_int]
         R.ref_attention_layer_cpu.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _F, _F, _F,
                                               _F, _F, C.c_int, _F]
@@ -211,6 +213,21 @@ def ref_rope(q: np.ndarray, k: np.ndarray, Hq: int, Hkv: int, head_dim: int, ste
     rows = qq.shape[0] if qq.ndim > 1 else 1
     rc = ref().ref_rope_cpu(_fp(qq), _fp(kk), rows, Hq, Hkv, head_dim, step, base)
     assert rc == 0
+    return qq, kk
+
+
+def ref_rope_cuda(q: np.ndarray, k: np.ndarray, Hq: int, Hkv: int, head_dim: int, step: int,
+                  base: float, yarn: dict | None = None):
+    """The reference's own rope_cuda (rope_cuda.cu:98-152) on one token row,
+    run on the current CUDA device; ``yarn`` = dict(factor, beta_fast,
+    beta_slow, orig_max_pos) turns its YaRN path on.  Needs a GPU."""
+    qq = np.ascontiguousarray(q, dtype=np.float32).reshape(-1).copy()
+    kk = np.ascontiguousarray(k, dtype=np.float32).reshape(-1).copy()
+    y = yarn or {}
+    rc = ref().ref_rope_cuda(_fp(qq), _fp(kk), Hq, Hkv, head_dim, step, base, 1 if yarn else 0,
+                             y.get("factor", 1.0), y.get("beta_fast", 32.0),
+                             y.get("beta_slow", 1.0), y.get("orig_max_pos", 4096))
+    assert rc == 0, f"ref_rope_cuda returned {rc}"
     return qq, kk
 
 

@@ -9,9 +9,12 @@
 // Every wrapper builds reference Tensors on the reference CPUAllocator and
 // calls the reference function unmodified:
 //   rope_cpu            hxinfer-engine/src/op/cpu/rope_cpu.cpp:5-39
+//   rope_cuda (YaRN)    hxinfer-engine/src/op/cuda/rope_cuda.cu:98-152, on a GPU
 //   softmax_cpu         hxinfer-engine/src/op/cpu/softmax_cpu.cpp:6-46
 //   AttentionLayer CPU  hxinfer-engine/src/layer/attention.cpp:37-88 (MHA only)
 //   PrefixCacheManager  hxinfer-engine/include/cache/prefix_cache.h:16-155
+#include <cuda_runtime.h>
+
 #include <cstring>
 #include <iostream>
 #include <memory>
@@ -69,6 +72,46 @@ int ref_rope_cpu(float* q, float* k, int rows, int head, int kv_head, int head_d
         return 0;
     } catch (const std::exception& e) {
         std::cerr << "ref_rope_cpu: " << e.what() << std::endl;
+        return 1;
+    }
+}
+
+// The reference's rope_cuda (rope_cuda.cu:98-152) on one token row, on the
+// current CUDA device: q [head*head_dim], k [kv_head*head_dim] fp32, rotated
+// in place by the reference's own kernels, with its YaRN settings when
+// use_yarn != 0 (multipliers rope_cuda.cu:13-30, attention factor :32-35).
+// Returns 0, 1 on a C++ exception, 2 on a CUDA error.
+int ref_rope_cuda(float* q, float* k, int head, int kv_head, int head_dim, int step, float base,
+                  int use_yarn, float factor, float beta_fast, float beta_slow, int orig_max_pos)
+{
+    try {
+        ModelConfig cfg{};
+        cfg.dim = head * head_dim;
+        cfg.head = head;
+        cfg.kv_head = kv_head;
+        cfg.rope_theta = base;
+        cfg.rope_use_yarn = use_yarn != 0;
+        cfg.rope_factor = factor;
+        cfg.rope_beta_fast = beta_fast;
+        cfg.rope_beta_slow = beta_slow;
+        cfg.rope_orig_max_pos = orig_max_pos;
+        auto cuda = std::make_shared<CUDAAllocator>();
+        auto tq = std::make_shared<Tensor>(cuda, std::vector<int>{1, head * head_dim},
+                                           DataType::kDataTypeFP32);
+        auto tk = std::make_shared<Tensor>(cuda, std::vector<int>{1, kv_head * head_dim},
+                                           DataType::kDataTypeFP32);
+        const size_t qb = tq->tensor_total_byte_size(), kb = tk->tensor_total_byte_size();
+        if (cudaMemcpy(tq->raw_data_ptr(), q, qb, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(tk->raw_data_ptr(), k, kb, cudaMemcpyHostToDevice) != cudaSuccess)
+            return 2;
+        rope_cuda(tq, tk, cfg, step, base);
+        if (cudaDeviceSynchronize() != cudaSuccess) return 2;
+        if (cudaMemcpy(q, tq->raw_data_ptr(), qb, cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy(k, tk->raw_data_ptr(), kb, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return 2;
+        return 0;
+    } catch (const std::exception& e) {
+        std::cerr << "ref_rope_cuda: " << e.what() << std::endl;
         return 1;
     }
 }
