@@ -257,26 +257,34 @@ def run_batched_decode(args):
     peer = None
     if p2p:
         # every rank's decode stores its rows straight into every rank's
-        # [LAYERS][NSEQ][HQ*HD] buffer (reference output layout, no assembly)
+        # [2][LAYERS][NSEQ][HQ*HD] buffer (reference output layout, no
+        # assembly); steps alternate between the two halves, so a rank writes
+        # a half again only after every rank has read it back (the step in
+        # between ends with an epoch exchange that follows that read)
         def exchange(blob):
             allb = [None] * world
             dist.all_gather_object(allb, blob)
             return allb
-        peer = kv.PeerGather(rank, world, LAYERS * NSEQ * HQ * HD * 2, exchange)
-        assembled = peer.view(torch.float16, shape=(LAYERS, NSEQ, HQ * HD))
+        layer_bytes = NSEQ * HQ * HD * 2
+        peer = kv.PeerGather(rank, world, 2 * LAYERS * layer_bytes, exchange)
+        assembled = peer.view(torch.float16, shape=(2, LAYERS, NSEQ, HQ * HD))
         out_rows = torch.tensor(seqs, dtype=torch.int32, device=dev)
         head0 = heads[0] * (HQ // HKV)
-        layer_bytes = NSEQ * HQ * HD * 2
         epoch = [0]
+        # Each layer's epoch exchange waits on a side stream, so the next
+        # layer's append and decode stream HBM while this layer's rows drain
+        # to the peers; a step ends when its last exchange has completed.
+        side = torch.cuda.Stream()
 
-    def attend(l, lens, timed_events=False):
+    def attend(l, lens, si, timed_events=False):
         if timed_events:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
         if p2p:
             epoch[0] += 1
-            cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer, out_offset=l * layer_bytes,
+            cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer,
+                                out_offset=((si % 2) * LAYERS + l) * layer_bytes,
                                 out_rows=out_rows, out_row_heads=HQ, out_head0=head0,
                                 workspace=ws)
         else:
@@ -285,7 +293,10 @@ def run_batched_decode(args):
             e1.record(stream)
             ev_pairs.append((e0, e1))
         if p2p:
-            peer.wait(epoch[0])
+            done = torch.cuda.Event()
+            done.record(stream)
+            side.wait_event(done)
+            peer.wait(epoch[0], stream=side)
         elif world > 1:
             dist.all_gather_into_tensor(gathered[l], out[l])
     seq_ids = torch.arange(n, dtype=torch.int32, device=dev)
@@ -302,7 +313,9 @@ def run_batched_decode(args):
         for l in range(LAYERS):
             cache.rope_append(l, k_in[l], v_in[l], seq_ids, pos, q=q_in[l], num_q_heads=hq,
                               table=table, q_out=q_rot[l])
-            attend(l, lens, timed_events)
+            attend(l, lens, si, timed_events)
+        if p2p:
+            stream.wait_stream(side)
 
     def barrier():
         if world > 1:
@@ -375,9 +388,10 @@ def run_batched_decode(args):
         for l in range(LAYERS):
             cache.rope_append(l, k_d[l], v_d[l], seq_ids, pos, q=q_d[l], num_q_heads=hq,
                               table=table, q_out=q_rot[l])
-            attend(l, lens)
+            attend(l, lens, si)
         if p2p:
-            out_h.copy_(assembled[:, r0:r1], non_blocking=True)
+            stream.wait_stream(side)
+            out_h.copy_(assembled[si % 2, :, r0:r1], non_blocking=True)
         else:
             out_h.copy_(out, non_blocking=True)
 
