@@ -9,18 +9,23 @@
 // over the paged cache (the rows' own K/V must already be appended).
 //
 // One CTA per (128-row query tile, q head); 192 threads:
-//   warp 4  TMA producer: Q tile once (2 boxes 128x64, 128-byte swizzle), then
-//           128-position K and V tiles (two cache blocks each) into a 2-stage
-//           ring; no multicast.
+//   warp 4  TMA producers: lane 0 the Q tile once (2 boxes 128x64, 128-byte
+//           swizzle) then a 3-stage ring of 128-position K tiles (two cache
+//           blocks each); lane 1 a 3-stage ring of V tiles; block-table rows
+//           are read one tile ahead; no multicast.
 //   warp 5  TMEM allocator (512 columns) and, lane 0, the MMA issuer:
-//           S_j = Q K_j^T  (M=128, N=128, K=16 x 8, fp16 -> fp32) into one of
-//           two TMEM S buffers, then O += P_j V_j (V as an MN-major operand)
-//           into the TMEM O accumulator; completion via tcgen05.commit.
+//           S_j = Q K_j^T  (M=128, N=128, K=16 x 8, fp16 -> fp32) into TMEM
+//           buffer j & 1, then O += P_j V_j with P_j read from that same
+//           buffer (V as an MN-major operand); order S_0, S_1, then PV_j,
+//           S_{j+2} for each j, so S_{j+1} runs during softmax j and S_{j+2}
+//           overwrites P_j only after PV_j (this thread's MMAs execute in
+//           order); completion via tcgen05.commit.
 //   warps 0-3  softmax: thread t owns query row t; reads S_j with tcgen05.ld,
 //           applies the causal mask, keeps a running max that only moves when
 //           it rises by more than 2^8 (then O in TMEM is rescaled), writes
-//           P_j = 2^(s - m) as fp16 into 128-byte-swizzled shared memory (the
-//           A operand of the next MMA), and in the end divides O by the row sum.
+//           P_j = 2^(s - m) as fp16 over S_j's own columns with tcgen05.st,
+//           and in the end divides O by the row sum, staged through an idle
+//           K stage for coalesced stores.
 // Key tiles above the diagonal are never loaded.  Every mbarrier wait is
 // bounded; TMEM is always released before exit.
 #include "hx_common.cuh"

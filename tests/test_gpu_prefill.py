@@ -1,5 +1,8 @@
 """K3 causal prefill (tcgen05) against the CPU oracle.
 
+The cases cover MHA and GQA groups of 2, 3, 4 and 7, lone and partial
+query tiles, and continuations after a cached prefix.
+
 Oracle: the reference prefills one token per forward call, so row i is the
 decode-step loop of attention.cpp:51-85 over positions [0, start+i]
 (oracle.prefill_attention).  Bar: |gpu - oracle| <= 2e-3 + 1e-2*|oracle|."""
@@ -70,3 +73,9 @@ def test_prefill_continuation(hx, oracle, start, n):
 
 def test_prefill_fp32_out(hx, oracle):
     run_prefill(hx, oracle, 4, 2, 10, 140, seed=9, out_dtype=torch.float32)
+
+
+@pytest.mark.parametrize("Hq,Hkv,start,n", [(32, 8, 0, 700), (16, 8, 40, 300), (12, 4, 0, 260)])
+def test_prefill_gqa_groups(hx, oracle, Hq, Hkv, start, n):
+    """GQA groups of 4 (LLaMA-3), 2 and 3, one with a cached prefix."""
+    run_prefill(hx, oracle, Hq, Hkv, start, n, seed=Hq + n)
