@@ -71,6 +71,8 @@ SIGNATURES = {
     "hx_snapshot_bytes": (C.c_size_t, [_P, _I]),
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
     "hx_kv_restore": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
+    "hx_kv_snapshot_layers": (_I, [C.POINTER(_P), _I, _I, _P, C.c_size_t, _P]),
+    "hx_kv_restore_layers": (_I, [C.POINTER(_P), _I, _I, _P, C.c_size_t, _P]),
     "hx_prefix_hash": (C.c_uint64, [C.POINTER(C.c_int32), C.c_size_t]),
     "hx_convert": (_I, [_P, _I, _P, _I, C.c_size_t, _P]),
     "hx_dist_handle_bytes": (C.c_size_t, []),

@@ -307,6 +307,38 @@ class KVCache:
                                    src.numel() * src.element_size(), _stream(stream)), "restore")
 
 
+def _handles(caches):
+    arr = (C.c_void_p * len(caches))(*[c.handle for c in caches])
+    return C.cast(arr, C.POINTER(C.c_void_p)), arr
+
+
+def snapshot_layers(caches, prefix_len: int, dst: torch.Tensor | None = None, stream=None):
+    """hx_kv_snapshot_layers: positions [0, prefix_len) of up to 64 one-layer
+    wrapped caches (one per model layer) copied into one buffer, layer i at
+    i * snapshot_bytes(prefix_len), in one launch."""
+    nbytes = len(caches) * caches[0].snapshot_bytes(prefix_len) if caches else 0
+    if dst is None:
+        dst = torch.empty(max(nbytes, 16), dtype=torch.uint8,
+                          device=torch.device("cuda", torch.cuda.current_device()))
+    _need_cuda(dst)
+    ptrs, keep = _handles(caches)
+    check(load().hx_kv_snapshot_layers(ptrs, len(caches), prefix_len, _ptr(dst),
+                                       dst.numel() * dst.element_size(), _stream(stream)),
+          "snapshot layers")
+    del keep
+    return dst
+
+
+def restore_layers(caches, prefix_len: int, src: torch.Tensor, stream=None):
+    """hx_kv_restore_layers: the inverse of snapshot_layers, one launch."""
+    _need_cuda(src)
+    ptrs, keep = _handles(caches)
+    check(load().hx_kv_restore_layers(ptrs, len(caches), prefix_len, _ptr(src),
+                                      src.numel() * src.element_size(), _stream(stream)),
+          "restore layers")
+    del keep
+
+
 class PeerGather:
     """This rank's gather endpoint (hx_dist_*): a device buffer that every
     rank's decode kernels write into over NVLink peer memory, plus the epoch

@@ -340,6 +340,22 @@ int hx_kv_snapshot(const hx_kv_cache* cache, int seq, int prefix_len, void* dst,
 int hx_kv_restore(hx_kv_cache* cache, int seq, int prefix_len, const void* src,
                   size_t src_bytes, hx_stream_t stream);
 
+/* hx_kv_snapshot over the layers of a model whose layers each hold their own
+ * cache (AttentionLayer keeps one [seq_len, kv_dim] K and V tensor per layer,
+ * attention.h:49-51, each wrapped by hx_kv_wrap): ONE launch copies
+ * positions [0, prefix_len) of every cache in caches[0 .. n_caches), into dst
+ * laid out [cache][K|V][kv_head][prefix_len][head_dim] fp16 -- the bytes of
+ * n_caches consecutive hx_kv_snapshot calls.  Every cache must come from
+ * hx_kv_wrap with the shape of caches[0], on the current device; at most 64
+ * caches per call.  Replaces the per-layer memcpy loop of
+ * PrefixCacheManager::store (prefix_cache.h:78-89). */
+int hx_kv_snapshot_layers(const hx_kv_cache* const* caches, int n_caches, int prefix_len,
+                          void* dst, size_t dst_bytes, hx_stream_t stream);
+/* The inverse copy, one launch (PrefixCacheManager::restore,
+ * prefix_cache.h:135-147); positions >= prefix_len are untouched. */
+int hx_kv_restore_layers(hx_kv_cache* const* caches, int n_caches, int prefix_len,
+                         const void* src, size_t src_bytes, hx_stream_t stream);
+
 /* ------------------------------------------------------------ weight loading */
 
 /* Converts n elements of src (device memory, src_dtype) into dst (device

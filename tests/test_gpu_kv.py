@@ -557,6 +557,59 @@ def test_snapshot_restore_qwen_shape(hx, plen):
         assert torch.equal(v1.view(torch.int16), v0.view(torch.int16))
 
 
+@pytest.mark.parametrize("layers,plen", [(28, 1), (28, 300), (64, 129), (3, 0)])
+def test_snapshot_layers_one_launch(hx, layers, plen):
+    """hx_kv_snapshot_layers over one-layer wrapped caches (the per-layer
+    caches of the model classes) is byte-identical to the per-cache
+    snapshots laid end to end; hx_kv_restore_layers puts the prefix back into
+    other caches and leaves their later positions untouched."""
+    Hkv, hd, cap = 4, 128, 321
+    gen = torch.Generator(device="cuda").manual_seed(layers * 1000 + plen)
+
+    def caches():
+        out = []
+        for _ in range(layers):
+            k = torch.randn(Hkv * cap * hd, device="cuda", generator=gen).half()
+            v = torch.randn(Hkv * cap * hd, device="cuda", generator=gen).half()
+            out.append(hx.KVCache.wrap(k, v, Hkv, hd, cap))
+        return out
+
+    src, dst = caches(), caches()
+    snap = hx.snapshot_layers(src, plen)
+    per = [c.snapshot(0, plen) for c in src]
+    torch.cuda.synchronize()
+    nb = src[0].snapshot_bytes(plen)
+    if plen:
+        assert torch.equal(snap[:layers * nb], torch.cat([p[:nb] for p in per]))
+    after = [(c._keep[0].clone(), c._keep[1].clone()) for c in dst]
+    hx.restore_layers(dst, plen, snap)
+    torch.cuda.synchronize()
+    hx.device_status()
+    for i in range(layers):
+        for kv in range(2):
+            got = dst[i]._keep[kv].view(Hkv, cap, hd)
+            want = src[i]._keep[kv].view(Hkv, cap, hd)
+            old = after[i][kv].view(Hkv, cap, hd)
+            assert torch.equal(got[:, :plen], want[:, :plen])
+            assert torch.equal(got[:, plen:], old[:, plen:])
+
+
+def test_snapshot_layers_refuses_mixed_caches(hx):
+    from hxinfer_b200._lib import HXError
+    k = torch.zeros(4 * 128 * 128, device="cuda", dtype=torch.float16)
+    a = hx.KVCache.wrap(k, k.clone(), 4, 128, 128)
+    b = hx.KVCache.wrap(k.clone(), k.clone(), 2, 128, 128)
+    with pytest.raises(HXError):
+        hx.snapshot_layers([a, b], 64)
+    many = [hx.KVCache.wrap(k, k.clone(), 4, 128, 128) for _ in range(65)]
+    with pytest.raises(HXError):
+        hx.snapshot_layers(many, 64)
+    pooled = make_cache(hx, 2, 4, 1, 128)
+    pooled.reserve(0, 128)
+    with pytest.raises(HXError):
+        hx.snapshot_layers([pooled], 64)
+
+
 def test_snapshot_rejects_unreserved_prefix(hx):
     cache = make_cache(hx, 1, 1, 1, 256)
     cache.reserve(0, 64)
