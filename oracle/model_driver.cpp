@@ -2,27 +2,37 @@
 // (test infrastructure only).
 //
 // Loads a model directory with the reference's DenseModelLoader
-// (model_loaders/src/dense_model_loader.cpp:20-158) and feeds it one token
-// per CausalLMModel::forward call (causal_lm_model.cpp:4-12), as the
-// reference's drivers do (demos/bench_1024.cpp:60-70): the input is a
-// one-element tensor holding the token id, the output the fp32 logits.
+// (model_loaders/src/dense_model_loader.cpp:20-158) and runs
+// CausalLMModel::forward (causal_lm_model.cpp:4-12) over a fixed token
+// sequence, the way the reference's drivers do (demos/bench_1024.cpp:60-70):
+// the input tensor holds token ids, the output the fp32 logits.
 // oracle/Makefile compiles this file twice:
 //   model_ref    the reference engine as it is (its own AttentionLayer,
-//                rope and attention kernels, CPU tensors and allocators);
-//   model_b200   the same engine sources with the hot-path headers replaced
-//                by this build's (HX_DROPIN defined), linked against
-//                libhxinfer.so / libhxkv.so: the drop-in a maintainer makes.
-// Both write the logits of every position, so the two runs compare row by
-// row.  model_b200 then checks PrefixCacheManager at model level: it stores
-// the first `prefix` positions, overwrites them by running other tokens at
-// those positions, restores, and runs the remaining tokens again; those
-// logits are appended to the output and must equal the first run's.
+//                TransformerLayer, SwigluLayer and CausalLMModel, its rope
+//                and attention kernels), one token per call;
+//   model_b200   the same engine sources with the hot-path headers and the
+//                n-row model classes replaced by this build's (HX_DROPIN),
+//                linked against libhxinfer.so / libhxkv.so: the drop-in a
+//                maintainer makes.  --chunk C feeds the prompt C tokens per
+//                call (the layers then prefill with the tcgen05 kernel).
 //
-// usage: model_driver <model_dir> <llama|qwen2> <tokens> <out.bin> [prefix]
+// usage: model_driver <model_dir> <llama|qwen2> <prompt> <out.bin | -> [options]
+//   --chunk C    prompt tokens per forward call (default 1; model_b200 only)
+//   --prefix P   model_b200: after the prompt, store the first P positions
+//                with PrefixCacheManager, overwrite them by running other
+//                tokens there, restore, and run positions P.. again one token
+//                per call; those logits are appended to the output
+//   --decode D   after the prompt, D single-token calls (timed)
+// The logits of every position go to out.bin (fp32 [rows][vocab]) unless it
+// is "-".  One JSON line on stdout gives the device time of the prompt pass
+// and of the decode calls (CUDA events on the legacy default stream around
+// the forward calls, host launch gaps included, as a caller sees them).
 #include <cuda_runtime.h>
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -42,13 +52,31 @@ static int token_at(int i, int vocab, int salt) { return (int)((i * 7919L + 13 +
 int main(int argc, char** argv)
 {
     if (argc < 5) {
-        std::fprintf(stderr, "usage: %s <model_dir> <llama|qwen2> <tokens> <out.bin> [prefix]\n", argv[0]);
+        std::fprintf(stderr, "usage: %s <model_dir> <llama|qwen2> <prompt> <out.bin|-> "
+                             "[--chunk C] [--prefix P] [--decode D]\n", argv[0]);
         return 2;
     }
     const std::string dir = argv[1];
     const ModelType type = std::string(argv[2]) == "qwen2" ? ModelType::Qwen2 : ModelType::LLaMA;
-    const int n = std::atoi(argv[3]);
-    const int prefix = argc > 5 ? std::atoi(argv[5]) : 0;
+    const int prompt = std::atoi(argv[3]);
+    const bool keep = std::strcmp(argv[4], "-") != 0;
+    int chunk = 1, prefix = 0, decode = 0;
+    for (int a = 5; a + 1 < argc; a += 2) {
+        if (!std::strcmp(argv[a], "--chunk")) chunk = std::atoi(argv[a + 1]);
+        else if (!std::strcmp(argv[a], "--prefix")) prefix = std::atoi(argv[a + 1]);
+        else if (!std::strcmp(argv[a], "--decode")) decode = std::atoi(argv[a + 1]);
+        else {
+            std::fprintf(stderr, "unknown option %s\n", argv[a]);
+            return 2;
+        }
+    }
+#ifndef HX_DROPIN
+    if (chunk != 1 || prefix) {
+        std::fprintf(stderr, "the reference engine takes one token per call and has no device prefix cache\n");
+        return 2;
+    }
+#endif
+    if (chunk < 1) chunk = 1;
 
     auto cpu_alloc = std::make_shared<CPUAllocator>();
     auto cuda_alloc = std::make_shared<CUDAAllocator>();
@@ -56,36 +84,66 @@ int main(int argc, char** argv)
     auto model = DenseModelLoader::load(dir, config, cpu_alloc, cuda_alloc, type);
     const int vocab = config.vocab_size;
 
-    auto in_cpu = std::make_shared<Tensor>(cpu_alloc, std::vector<int>{1}, DataType::kDataTypeFP32);
-    auto in_gpu = std::make_shared<Tensor>(cuda_alloc, std::vector<int>{1}, DataType::kDataTypeFP32);
-    auto logits = std::make_shared<Tensor>(cuda_alloc, std::vector<int>{1, vocab}, DataType::kDataTypeFP32);
-    in_gpu->tensor_set_device_type(DeviceType::kDeviceCUDA);
-    logits->tensor_set_device_type(DeviceType::kDeviceCUDA);
-
-    FILE* out = std::fopen(argv[4], "wb");
-    if (!out) {
+    FILE* out = keep ? std::fopen(argv[4], "wb") : nullptr;
+    if (keep && !out) {
         std::perror(argv[4]);
         return 1;
     }
-    std::vector<float> row(vocab);
-    auto step = [&](int token, int pos, bool keep) -> bool {
-        in_cpu->tensor_data_ptr<int>()[0] = token;
-        cudaMemcpy(in_gpu->raw_data_ptr(), in_cpu->raw_data_ptr(), sizeof(int), cudaMemcpyHostToDevice);
-        model->forward(in_gpu, logits, pos);
-        if (!keep) return true;
-        if (cudaMemcpy(row.data(), logits->raw_data_ptr(), vocab * sizeof(float), cudaMemcpyDeviceToHost) !=
-            cudaSuccess)
-            return false;
-        return std::fwrite(row.data(), sizeof(float), vocab, out) == (size_t)vocab;
+    std::vector<float> rows;
+    // One forward call over tokens [pos, pos+n) of sequence `salt`; with `all`
+    // the output holds every row's logits (n * vocab), else the last row's.
+    struct Io {
+        std::shared_ptr<Tensor> in_cpu, in_gpu, logits;
     };
-
-    for (int i = 0; i < n; ++i)
-        if (!step(token_at(i, vocab, 0), i, true)) {
-            std::fprintf(stderr, "forward %d failed: %s\n", i, cudaGetErrorString(cudaGetLastError()));
+    std::map<int, Io> io;  // by tokens per call, allocated once
+    auto step = [&](int pos, int n, int salt, bool write) -> bool {
+        const bool all = n > 1;
+        Io& b = io[n];
+        if (!b.in_cpu) {
+            b.in_cpu = std::make_shared<Tensor>(cpu_alloc, std::vector<int>{n}, DataType::kDataTypeFP32);
+            b.in_gpu = std::make_shared<Tensor>(cuda_alloc, std::vector<int>{n}, DataType::kDataTypeFP32);
+            b.logits = std::make_shared<Tensor>(cuda_alloc, std::vector<int>{all ? n : 1, vocab},
+                                                DataType::kDataTypeFP32);
+            b.in_gpu->tensor_set_device_type(DeviceType::kDeviceCUDA);
+            b.logits->tensor_set_device_type(DeviceType::kDeviceCUDA);
+        }
+        auto& in_cpu = b.in_cpu;
+        auto& in_gpu = b.in_gpu;
+        auto& logits = b.logits;
+        for (int i = 0; i < n; ++i) in_cpu->tensor_data_ptr<int>()[i] = token_at(pos + i, vocab, salt);
+        cudaMemcpy(in_gpu->raw_data_ptr(), in_cpu->raw_data_ptr(), n * sizeof(int), cudaMemcpyHostToDevice);
+        model->forward(in_gpu, logits, pos);
+        if (!write || !out) return true;
+        rows.resize((size_t)n * vocab);
+        if (cudaMemcpy(rows.data(), logits->raw_data_ptr(), rows.size() * sizeof(float),
+                       cudaMemcpyDeviceToHost) != cudaSuccess)
+            return false;
+        return std::fwrite(rows.data(), sizeof(float), rows.size(), out) == rows.size();
+    };
+    // With one token per call every position's logits are written; with
+    // chunks, each call writes all of its rows.
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&e2);
+    cudaEventRecord(e0, 0);
+    for (int pos = 0; pos < prompt; pos += chunk) {
+        const int n = std::min(chunk, prompt - pos);
+        if (!step(pos, n, 0, true)) {
+            std::fprintf(stderr, "forward at %d failed: %s\n", pos, cudaGetErrorString(cudaGetLastError()));
             return 1;
         }
+    }
+    cudaEventRecord(e1, 0);
+    for (int t = 0; t < decode; ++t)
+        if (!step(prompt + t, 1, 0, false)) return 1;
+    cudaEventRecord(e2, 0);
+    cudaEventSynchronize(e2);
+    float prompt_ms = 0, decode_ms = 0;
+    cudaEventElapsedTime(&prompt_ms, e0, e1);
+    cudaEventElapsedTime(&decode_ms, e1, e2);
 #ifdef HX_DROPIN
-    if (prefix > 0 && prefix < n) {
+    if (prefix > 0 && prefix < prompt) {
         std::vector<int> toks(prefix);
         for (int i = 0; i < prefix; ++i) toks[i] = token_at(i, vocab, 0);
         PrefixCacheManager mgr(cpu_alloc, config);
@@ -94,20 +152,24 @@ int main(int argc, char** argv)
             std::fprintf(stderr, "prefix lookup missed\n");
             return 1;
         }
-        for (int i = 0; i < prefix; ++i) step(token_at(i, vocab, 1), i, false);  // other tokens
+        for (int i = 0; i < prefix; ++i) step(i, 1, 1, false);  // other tokens at those positions
         mgr.restore(toks, *model);
-        for (int i = prefix; i < n; ++i)
-            if (!step(token_at(i, vocab, 0), i, true)) return 1;
+        for (int i = prefix; i < prompt; ++i)
+            if (!step(i, 1, 0, true)) return 1;
     }
+    const char* build = "b200";
 #else
-    (void)prefix;
+    const char* build = "ref";
 #endif
-    std::fclose(out);
+    if (out) std::fclose(out);
     const cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         std::fprintf(stderr, "device error: %s\n", cudaGetErrorString(e));
         return 1;
     }
-    std::printf("model_driver: %d positions of %d logits written\n", n, vocab);
+    std::printf("{\"build\": \"%s\", \"layers\": %d, \"dim\": %d, \"prompt\": %d, \"chunk\": %d, "
+                "\"prompt_ms\": %.4f, \"decode_steps\": %d, \"decode_ms_per_token\": %.5f}\n",
+                build, config.layer, config.dim, prompt, chunk, prompt_ms, decode,
+                decode ? decode_ms / decode : 0.0f);
     return 0;
 }

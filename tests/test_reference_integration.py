@@ -4,8 +4,9 @@ A maintainer replaces the reference's hot-path headers with this build's, at
 the same paths (the reference's layer headers include their siblings by
 relative name, so the files themselves must be replaced; an include path
 placed first would not shadow them), removes the reference's hot-path
-sources, and links the rest of the engine against libhxinfer.so and
-libhxkv.so.  This test does exactly that in a scratch directory: every
+sources, compiles this build's n-row TransformerLayer / SwigluLayer /
+CausalLMModel (hxinfer_b200/cpp/engine) in their place, and links the rest
+of the engine against libhxinfer.so and libhxkv.so.  This test does exactly that in a scratch directory: every
 remaining engine source and the reference's DenseModelLoader
 (model_loaders/src/dense_model_loader.cpp, over this build's
 SafetensorsMultiReader) are compiled with nvcc and linked into one shared
@@ -28,13 +29,17 @@ NVCC = "/usr/local/cuda/bin/nvcc"
 
 # this build's header -> the reference header it replaces (same relative path)
 REPLACED_HEADERS = ["base/allocator.h", "base/buffer.h", "base/config.h", "tensor/tensor.h",
-                    "op/math_ops.h", "layer/layer.h", "layer/attention.h", "cache/prefix_cache.h"]
+                    "op/math_ops.h", "layer/layer.h", "layer/attention.h", "cache/prefix_cache.h",
+                    "layer/swiglu.h", "layer/transformer.h", "model/causal_lm_model.h"]
 REPLACED_LOADER_HEADERS = ["safetensors_loader.h"]
 # reference sources whose functions libhxinfer.so provides
 REMOVED_SOURCES = ["op/cpu/rope_cpu.cpp", "op/rope_tensor.cpp", "op/cuda/rope_cuda.cu",
                    "op/cuda/attention_score_cuda.cu", "op/cuda/bias_add.cu", "layer/attention.cpp",
                    "base/allocator_cpu.cpp", "base/allocator_cuda.cu", "base/buffer.cpp",
-                   "tensor/tensor.cpp"]
+                   "tensor/tensor.cpp", "layer/swiglu.cpp", "layer/transformer.cpp",
+                   "model/causal_lm_model.cpp"]
+# this build's n-row replacements for the last three, compiled with the engine
+ENGINE_SOURCES = sorted(glob.glob(os.path.join(PKG, "cpp", "engine", "*", "*.cpp")))
 REMOVED_LOADER_SOURCES = ["safetensors_loader.cpp"]
 
 
@@ -72,6 +77,8 @@ def test_reference_engine_builds_and_links_over_this_build(tmp_path):
     for r in REMOVED_SOURCES:
         assert r in sources, r
     jobs = [(os.path.join(src_root, s), []) for s in sources if s not in REMOVED_SOURCES]
+    assert len(ENGINE_SOURCES) == 3, ENGINE_SOURCES
+    jobs += [(s, []) for s in ENGINE_SOURCES]
     json_inc = nlohmann_include()
     loader_root = os.path.join(REFERENCE, "model_loaders", "src")
     if json_inc:
@@ -81,7 +88,8 @@ def test_reference_engine_builds_and_links_over_this_build(tmp_path):
 
     def compile_one(job):
         src, extra = job
-        out = obj / (os.path.relpath(src, REFERENCE).replace(os.sep, "_") + ".o")
+        base = ROOT if src.startswith(PKG) else REFERENCE
+        out = obj / (os.path.relpath(src, base).replace(os.sep, "_") + ".o")
         cmd = [NVCC, "-std=c++17", "-O1", "-Xcompiler", "-fPIC", "-x", "cu",
                "-gencode", "arch=compute_100a,code=sm_100a", f"-I{inc}", f"-I{ml}",
                f"-I{os.path.join(ROOT, 'include')}", *extra, "-c", src, "-o", str(out)]
