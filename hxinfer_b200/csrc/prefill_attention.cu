@@ -352,7 +352,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
             const int b = j & 1;
-            if (!pf_wait(sm, &sm.s_full[b], (j >> 1) & 1, p.status)) {
+            // tcgen05.ld/st are warp-collective (.sync.aligned): every branch
+            // around them is made warp-uniform, wait outcomes included
+            if (!__all_sync(0xffffffffu, pf_wait(sm, &sm.s_full[b], (j >> 1) & 1, p.status))) {
                 ok = false;
                 break;
             }
@@ -380,27 +382,33 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
                 for (int e = 0; e < w; ++e) mx8[e] = fmaxf(mx8[e], mx8[e + w]);
             const float mt = mx8[0] * sc;  // the scale is positive: the max commutes with it
-            if (mt > m_run + 8.f) {
-                const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
-                if (j >= 1 && alpha < 1.f) {
-                    // O must be stable: P_{j-1} V_{j-1} has finished
-                    if (!pf_wait(sm, &sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t oaddr = lane_base + 256;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        float ov[32];
-                        tmem_ld32(oaddr + 32 * c, ov);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-                        tmem_st32(oaddr + 32 * c, ov);
-                    }
-                    tmem_st_wait();
+            // Lazy rescale: a row moves its reference max only when the max
+            // grew by more than 2^8.  The decision is per row, the O update
+            // per warp: when any row of the warp rescales, the whole warp
+            // loads and stores its O rows, the others with alpha = 1 (exact).
+            const bool grow = mt > m_run + 8.f;
+            const float alpha = grow ? fast_exp2(m_run - mt) : 1.f;  // 0 when m_run = -inf
+            if (j >= 1 && __any_sync(0xffffffffu, alpha < 1.f)) {
+                // O must be stable: P_{j-1} V_{j-1} has finished
+                if (!__all_sync(0xffffffffu,
+                                pf_wait(sm, &sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status))) {
+                    ok = false;
+                    break;
                 }
+                tc_fence_after();
+                const uint32_t oaddr = lane_base + 256;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float ov[32];
+                    tmem_ld32(oaddr + 32 * c, ov);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                    tmem_st32(oaddr + 32 * c, ov);
+                }
+                tmem_st_wait();
+            }
+            if (grow) {
                 l *= alpha;
                 m_run = mt;
             }
@@ -424,7 +432,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 // V rows past the last needed key may hold stale bytes: zero
                 // this thread's row so 0 * garbage cannot reach O.
                 const int vs = j % kPfVStages;
-                if (!pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status)) {
+                if (!__all_sync(0xffffffffu, pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status))) {
                     ok = false;
                     break;
                 }
@@ -441,8 +449,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.p_full[b]);
         }
-        const bool have_o =
-            ok && nk > 0 && pf_wait(sm, &sm.pv_done[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status);
+        const bool have_o = __all_sync(
+            0xffffffffu, ok && nk > 0 && pf_wait(sm, &sm.pv_done[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status));
         // Epilogue: O / l goes through shared memory (the K ring is idle once
         // the last PV has completed: every S MMA completed before it) so the
         // global stores are coalesced.  Row t is staged at t * row_bytes with

@@ -158,18 +158,22 @@ int main(int argc, char** argv)
             if (!step(i, 1, 0, true)) return 1;
     }
     const char* build = "b200";
+    const int status = hx_device_status(0);  // a kernel's recorded failure, HX_OK if none
 #else
     const char* build = "ref";
+    const int status = 0;
 #endif
     if (out) std::fclose(out);
     const cudaError_t e = cudaDeviceSynchronize();
+    if (status) std::fprintf(stderr, "device status %d: a kernel recorded a failure\n", status);
     if (e != cudaSuccess) {
         std::fprintf(stderr, "device error: %s\n", cudaGetErrorString(e));
         return 1;
     }
     std::printf("{\"build\": \"%s\", \"layers\": %d, \"dim\": %d, \"prompt\": %d, \"chunk\": %d, "
-                "\"prompt_ms\": %.4f, \"decode_steps\": %d, \"decode_ms_per_token\": %.5f}\n",
+                "\"prompt_ms\": %.4f, \"decode_steps\": %d, \"decode_ms_per_token\": %.5f, "
+                "\"device_status\": %d}\n",
                 build, config.layer, config.dim, prompt, chunk, prompt_ms, decode,
-                decode ? decode_ms / decode : 0.0f);
-    return 0;
+                decode ? decode_ms / decode : 0.0f, status);
+    return status ? 1 : 0;
 }

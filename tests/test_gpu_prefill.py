@@ -28,12 +28,16 @@ def hx():
     return kv
 
 
-def run_prefill(hx, oracle, Hq, Hkv, start, n, seed, out_dtype=torch.float16, layers=2, layer=1):
+def run_prefill(hx, oracle, Hq, Hkv, start, n, seed, out_dtype=torch.float16, layers=2, layer=1,
+                qkv=None):
     rng = np.random.default_rng(seed)
     total = start + n
-    kc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
-    vc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
-    q = oracle.f16(rng.standard_normal((n, Hq * 128)))
+    if qkv is None:
+        kc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
+        vc = oracle.f16(rng.standard_normal((total, Hkv * 128)))
+        q = oracle.f16(rng.standard_normal((n, Hq * 128)))
+    else:
+        q, kc, vc = qkv
     cache = hx.KVCache(layers, Hkv, 128, 3, total + 64)
     seq = 2  # not the first sequence: exercises the block table
     cache.reserve(0, 64)
@@ -79,3 +83,26 @@ def test_prefill_fp32_out(hx, oracle):
 def test_prefill_gqa_groups(hx, oracle, Hq, Hkv, start, n):
     """GQA groups of 4 (LLaMA-3), 2 and 3, one with a cached prefix."""
     run_prefill(hx, oracle, Hq, Hkv, start, n, seed=Hq + n)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_prefill_rows_rescale_apart(hx, oracle, out_dtype):
+    """Rows of one warp that move their running max at different key tiles.
+    Even query rows are +12u and odd rows -12u for a unit vector u; keys are
+    small except that every key from position 128 on is +12u.  At the second
+    key tile the even rows' max jumps by about 2^18 (they rescale O) and the
+    odd rows' does not, so within each warp some rows rescale and others keep
+    their max: the O update must stay warp-collective."""
+    rng = np.random.default_rng(11)
+    Hq = Hkv = 2
+    n = 384
+    u = rng.standard_normal(128)
+    u /= np.linalg.norm(u)
+    q = 0.05 * rng.standard_normal((n, Hq, 128))
+    q[0::2] += 12 * u
+    q[1::2] -= 12 * u
+    kc = 0.05 * rng.standard_normal((n, Hkv, 128))
+    kc[128:] += 12 * u
+    vc = rng.standard_normal((n, Hkv, 128))
+    qkv = tuple(oracle.f16(a.reshape(a.shape[0], -1)) for a in (q, kc, vc))
+    run_prefill(hx, oracle, Hq, Hkv, 0, n, seed=0, out_dtype=out_dtype, qkv=qkv)
