@@ -8,6 +8,7 @@
     python -m hxinfer_b200.profile_case c5 --len 2048 --new 256 --steps 128 --layers 28 --conts 32
     python -m hxinfer_b200.profile_case qkv --shape qwen --seqs 1 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case convert --mib 1024 --iters 10
+    torchrun --nproc-per-node 8 -m hxinfer_b200.profile_case oproj --seqs 64 --iters 50
 
 Each case fills a cache with N(0,1) fp16, runs the kernels `iters` times and
 prints one JSON line with the CUDA-event time per iteration and the
@@ -358,7 +359,7 @@ def qkv_case(a):
            for m in (hq, hkv, hkv)] for _ in range(layers)]
     bs = [(torch.randn((m * hd,), generator=g, device=dev) * 0.02).half() for m in (hq, hkv, hkv)]
     x = torch.randn((n, hidden), generator=g, device=dev).half()
-    cache = kv.KVCache(layers, hkv, hd, n, 64)
+    cache = kv.KVCache(layers, hkv, hd, n, 64, overlap=a.overlap)
     for s in range(n):
         cache.reserve(s, 64)
     table = kv.RopeTable(hd, 64, theta)
@@ -398,7 +399,7 @@ def qkv_case(a):
             res[name] = 1e3 * e0.elapsed_time(e1) / (a.iters * layers)
     kv.device_status()
     wbytes = (hq + 2 * hkv) * hd * hidden * 2
-    print(json.dumps({"case": "qkv", "shape": a.shape, "tokens": n, "layers": layers,
+    print(json.dumps({"case": "qkv", "shape": a.shape, "tokens": n, "layers": layers, "overlap": a.overlap,
                       "weight_bytes_per_layer": wbytes,
                       "fused_us_per_layer": res["fused"], "chain_us_per_layer": res["cublas_chain"],
                       "fused_gbs": wbytes / (res["fused"] * 1e-6) / 1e9,
@@ -434,9 +435,87 @@ def convert_case(a):
     print(json.dumps({"case": "convert", "mib": a.mib, **res}))
 
 
+def oproj_case(a):
+    """The output projection after a sharded decode or prefill, two ways, on
+    WORLD_SIZE ranks (torchrun, one GPU each), LLaMA-3-8B shape (dim 4096,
+    32 q heads).  Each rank holds the attention rows of its q-head slice,
+    [rows, 4096 / world].
+      replicated:    all-gather the slices, then every rank runs the full
+                     [rows, 4096] x [4096, 4096]^T projection (the reference's
+                     o_proj, attention.cpp:87, after the gather);
+      row-parallel:  each rank multiplies its slice by its [4096, 4096 / world]
+                     column block of the weight, then an all-reduce sums the
+                     [rows, 4096] partials.
+    Both use cuBLAS (torch.matmul) and NCCL; device time per layer with CUDA
+    events, the max over ranks.  `seqs` rows for a decode step; --len rows for
+    a prefill when given."""
+    import os
+
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+    dev = torch.device("cuda")
+    dim, layers = 4096, a.layers
+    if dim % world:
+        raise ValueError("world must divide 4096")
+    sl = dim // world
+    g = torch.Generator(device="cuda")
+    g.manual_seed(17 + rank)
+    res = {}
+    for rows in sorted({a.seqs, a.len}):
+        w_full = [(torch.randn((dim, dim), generator=g, device=dev) * 0.02).half() for _ in range(layers)]
+        w_cols = [w[:, rank * sl:(rank + 1) * sl].contiguous() for w in w_full]
+        x_sl = torch.randn((rows, sl), generator=g, device=dev).half()
+        x_full = torch.empty((rows, dim), dtype=torch.float16, device=dev)
+        gathered = torch.empty((world, rows, sl), dtype=torch.float16, device=dev)
+        y = torch.empty((rows, dim), dtype=torch.float16, device=dev)
+
+        def replicated():
+            for l in range(layers):
+                if world > 1:
+                    dist.all_gather_into_tensor(gathered, x_sl)
+                    x_full.copy_(gathered.permute(1, 0, 2).reshape(rows, dim))
+                else:
+                    x_full.copy_(x_sl)
+                torch.matmul(x_full, w_full[l].t(), out=y)
+
+        def row_parallel():
+            for l in range(layers):
+                torch.matmul(x_sl, w_cols[l].t(), out=y)
+                if world > 1:
+                    dist.all_reduce(y)
+
+        for name, fn in (("replicated", replicated), ("row_parallel", row_parallel)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            us = torch.tensor([1e3 * e0.elapsed_time(e1) / (a.iters * layers)], device=dev)
+            if world > 1:
+                dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            res[f"{name}_us_rows{rows}"] = us.item()
+        del w_full, w_cols
+    if rank == 0:
+        print(json.dumps({"case": "oproj", "world": world, "dim": dim, "layers": layers,
+                          "slice": sl, **res}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "c5", "qkv", "convert"])
+    ap.add_argument("case", choices=["decode", "snapshot", "prefill", "c2", "c5", "qkv", "convert", "oproj"])
     ap.add_argument("--mib", type=int, default=1024, help="convert: MiB of source data")
     ap.add_argument("--shape", default="llama3", choices=sorted(SHAPES))
     ap.add_argument("--seqs", type=int, default=16)
@@ -450,9 +529,11 @@ def main():
     ap.add_argument("--overlap", action="store_true",
                     help="programmatic dependent launch of append -> decode (HX_KV_OVERLAP_LAUNCH)")
     a = ap.parse_args()
-    torch.cuda.set_device(0)
+    if a.case != "oproj":  # oproj picks LOCAL_RANK's device itself
+        torch.cuda.set_device(0)
     {"decode": decode_case, "snapshot": snapshot_case, "prefill": prefill_case,
-     "c2": c2_case, "c5": c5_case, "qkv": qkv_case, "convert": convert_case}[a.case](a)
+     "c2": c2_case, "c5": c5_case, "qkv": qkv_case, "convert": convert_case,
+     "oproj": oproj_case}[a.case](a)
 
 
 if __name__ == "__main__":
