@@ -170,18 +170,10 @@ __global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
         const int d = 16 * qtr + (lr & 15) + (lr >= 16 ? 64 : 0);
         wrow[r] = reinterpret_cast<const uint4*>(wslot + (int64_t)d * hidden);
     }
-    // The weights do not depend on the previous kernel: before waiting for
-    // it, ask L2 for this CTA's whole slice (lane r of each warp one of the
-    // warp's four rows, hidden * 2 bytes in one bulk prefetch), so every
-    // byte the CTA will read is in flight from the start; the loads below
-    // then find their lines in L2 or on the way.
-    if (lane < 4) {
-        const int lr = 4 * warp + lane;
-        const int d = 16 * qtr + (lr & 15) + (lr >= 16 ? 64 : 0);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wslot + (int64_t)d * hidden),
-                     "r"((uint32_t)hidden * 2u)
-                     : "memory");
-    }
+    // the weights do not depend on the previous kernel: start them streaming
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        if (lane < chunks) asm volatile("prefetch.global.L2 [%0];" ::"l"(wrow[r] + lane));
 
     pdl_wait();  // x, seq_ids and positions come from the previous kernel
     for (int e = threadIdx.x; e < nt * chunks; e += kQkvThreads) {
