@@ -440,15 +440,18 @@ def oproj_case(a):
     WORLD_SIZE ranks (torchrun, one GPU each), LLaMA-3-8B shape (dim 4096,
     32 q heads).  Each rank holds the attention rows of its q-head slice,
     [rows, 4096 / world].
-      replicated:    all-gather the slices, then every rank runs the full
-                     [rows, 4096] x [4096, 4096]^T projection (the reference's
-                     o_proj, attention.cpp:87, after the gather);
+      replicated:    all-gather the slices (NCCL), then every rank runs the
+                     full [rows, 4096] x [4096, 4096]^T projection (the
+                     reference's o_proj, attention.cpp:87, after the gather);
+                     `replicated_gemm` is its GEMM alone, i.e. the cost when
+                     the gather is fused into the decode kernels;
       row-parallel:  each rank multiplies its slice by its [4096, 4096 / world]
-                     column block of the weight, then an all-reduce sums the
-                     [rows, 4096] partials.
-    Both use cuBLAS (torch.matmul) and NCCL; device time per layer with CUDA
-    events, the max over ranks.  `seqs` rows for a decode step; --len rows for
-    a prefill when given."""
+                     column block of the weight, then an all-reduce (NCCL)
+                     sums the [rows, 4096] partials.
+    Each arm runs `layers` layers (weights streamed from HBM) captured in one
+    CUDA graph; device time per layer with CUDA events over `iters` replays,
+    the max over ranks.  `seqs` rows for a decode step, `len` rows for a
+    prefill."""
     import os
 
     import torch.distributed as dist
@@ -482,24 +485,39 @@ def oproj_case(a):
                     x_full.copy_(x_sl)
                 torch.matmul(x_full, w_full[l].t(), out=y)
 
+        def replicated_gemm():
+            for l in range(layers):
+                torch.matmul(x_full, w_full[l].t(), out=y)
+
         def row_parallel():
             for l in range(layers):
                 torch.matmul(x_sl, w_cols[l].t(), out=y)
                 if world > 1:
                     dist.all_reduce(y)
 
-        for name, fn in (("replicated", replicated), ("row_parallel", row_parallel)):
-            for _ in range(3):
+        for name, fn in (("replicated", replicated), ("replicated_gemm", replicated_gemm),
+                         ("row_parallel", row_parallel)):
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
                 fn()
+            graph.replay()
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(a.iters):
-                fn()
+                graph.replay()
             e1.record()
             torch.cuda.synchronize()
+            del graph  # released before the process group (it holds NCCL calls)
             us = torch.tensor([1e3 * e0.elapsed_time(e1) / (a.iters * layers)], device=dev)
             if world > 1:
                 dist.all_reduce(us, op=dist.ReduceOp.MAX)
@@ -507,8 +525,9 @@ def oproj_case(a):
         del w_full, w_cols
     if rank == 0:
         print(json.dumps({"case": "oproj", "world": world, "dim": dim, "layers": layers,
-                          "slice": sl, **res}))
+                          "slice": sl, "timing": "CUDA graph, max over ranks", **res}))
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 
