@@ -2,6 +2,7 @@
 
     python -m hxinfer_b200.profile_case decode  --shape llama3 --seqs 16 --len 8192 --layers 1 --iters 5
     python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
+    python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --len 16874 --layers 8 --iters 20
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
@@ -26,7 +27,10 @@ import torch
 
 from . import kv
 
-SHAPES = {"llama3": (32, 8, 5e5), "qwen": (28, 4, 1e6), "llama2": (32, 32, 1e4)}
+# (q heads, kv heads, rope theta); llama3_kvhead is one rank's shard of the
+# LLaMA-3 attention when 8 ranks split the kv heads (one kv head, 4 q heads)
+SHAPES = {"llama3": (32, 8, 5e5), "qwen": (28, 4, 1e6), "llama2": (32, 32, 1e4),
+          "llama3_kvhead": (4, 1, 5e5)}
 
 
 def decode_case(a):
