@@ -4,13 +4,15 @@ Default workload — batched decode attention, LLaMA-3-8B attention shape:
 32 q heads, 8 kv heads, head_dim 128, fp16 cache, 32 layers, 64 sequences
 with cached lengths drawn once (seed 20261201) uniform in [512, 32768], K/V
 ~ N(0,1).  One step = for every layer: fused RoPE+append of each sequence's
-new token (K1) then split-K decode attention over the grown cache (K2 +
-combine), i.e. one decode token for each of the 64 sequences.  Metric:
+new token and split-K decode attention over the grown cache, in one launch
+per layer (hx_append_decode_attention; ``--separate``: K1 then K2 as two
+launches), i.e. one decode token for each of the 64 sequences.  Metric:
 aggregate decode tok/s; the decode kernel's achieved HBM GB/s is in
 ``roofline``.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--collective p2p|nccl] [--overlap] [--no-cpu-baseline] [--no-c1-32k]
+                  [--collective p2p|nccl] [--separate] [--overlap] [--no-cpu-baseline]
+                  [--no-c1-32k]
 
 At N=1 the same JSON line also carries ``c1_32k``: batch-1 decode on the
 Qwen2.5-7B attention shape (28 q heads, 4 kv heads, head_dim 128) over
@@ -276,19 +278,31 @@ def run_batched_decode(args):
         # to the peers; a step ends when its last exchange has completed.
         side = torch.cuda.Stream()
 
-    def attend(l, lens, si, timed_events=False):
+    def attend(l, si, q, k, v, timed_events=False):
+        """One layer of a decode step: the new tokens' RoPE + append and the
+        decode attention, in one launch (hx_append_decode_attention), or with
+        --separate as K1 then K2 (hx_rope_append, hx_decode_attention)."""
+        pos, lens = pos_tab[si], len_tab[si]
+        if args.separate:
+            cache.rope_append(l, k, v, seq_ids, pos, q=q, num_q_heads=hq, table=table,
+                              q_out=q_rot[l])
         if timed_events:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
         if p2p:
             epoch[0] += 1
-            cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer,
-                                out_offset=((si % 2) * LAYERS + l) * layer_bytes,
-                                out_rows=out_rows, out_row_heads=HQ, out_head0=head0,
-                                workspace=ws)
-        else:
+            place = dict(out_offset=((si % 2) * LAYERS + l) * layer_bytes, out_rows=out_rows,
+                         out_row_heads=HQ, out_head0=head0, workspace=ws)
+            if args.separate:
+                cache.decode_gather(l, q_rot[l], seq_ids, lens, hq, peer, **place)
+            else:
+                cache.append_decode_gather(l, q, k, v, seq_ids, lens, hq, peer, table=table, **place)
+        elif args.separate:
             cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
+        else:
+            cache.append_decode(l, q, k, v, seq_ids, lens, hq, table=table, out=out[l],
+                                workspace=ws)
         if timed_events:
             e1.record(stream)
             ev_pairs.append((e0, e1))
@@ -309,11 +323,8 @@ def run_batched_decode(args):
     ev_pairs = []
 
     def step(si, timed_events=False):
-        pos, lens = pos_tab[si], len_tab[si]
         for l in range(LAYERS):
-            cache.rope_append(l, k_in[l], v_in[l], seq_ids, pos, q=q_in[l], num_q_heads=hq,
-                              table=table, q_out=q_rot[l])
-            attend(l, lens, si, timed_events)
+            attend(l, si, q_in[l], k_in[l], v_in[l], timed_events)
         if p2p:
             stream.wait_stream(side)
 
@@ -361,10 +372,14 @@ def run_batched_decode(args):
     dec_ms = [a.elapsed_time(b) for a, b in ev_pairs]
     dec_avg_ms = max_over_ranks(sum(dec_ms) / len(dec_ms))
 
-    # algorithmic bytes of one decode launch (this rank): K+V read over the
-    # grown cache + q read + out write, averaged over the timed steps
+    # algorithmic bytes of one decode call (this rank): K+V read over the
+    # grown cache + q read + out write, averaged over the timed steps; the
+    # one-launch form also reads the new k and v rows and writes them to the
+    # cache
     mean_len = float(np.mean([np.sum(my_len + s + 1) for s in range(W, W + K)]))
     dec_bytes = 2 * mean_len * hkv * HD * 2 + 2 * n * hq * HD * 2
+    if not args.separate:
+        dec_bytes += 2 * (2 * n * hkv * HD * 2)
     achieved = dec_bytes / (dec_avg_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
 
@@ -384,11 +399,8 @@ def run_batched_decode(args):
         q_d.copy_(q_h, non_blocking=True)
         k_d.copy_(k_h, non_blocking=True)
         v_d.copy_(v_h, non_blocking=True)
-        pos, lens = pos_tab[si], len_tab[si]
         for l in range(LAYERS):
-            cache.rope_append(l, k_d[l], v_d[l], seq_ids, pos, q=q_d[l], num_q_heads=hq,
-                              table=table, q_out=q_rot[l])
-            attend(l, lens, si)
+            attend(l, si, q_d[l], k_d[l], v_d[l])
         if p2p:
             stream.wait_stream(side)
             out_h.copy_(assembled[si % 2, :, r0:r1], non_blocking=True)
@@ -437,7 +449,11 @@ def run_batched_decode(args):
                        "l2": "inputs larger than L2 (KV cache >> 126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "decode_attention_kernel + decode_combine_kernel (one call)",
+                         "kernel": ("decode_attention_kernel (+ decode_combine_kernel when not "
+                                    "folded), one hx_decode_attention call" if args.separate else
+                                    "decode_attention_kernel with the new tokens' RoPE + append "
+                                    "(+ decode_combine_kernel when not folded), one "
+                                    "hx_append_decode_attention call"),
                          "bytes_per_launch": dec_bytes, "avg_launch_ms": dec_avg_ms,
                          "traffic": DECODE_TRAFFIC_RATIO * dec_bytes,
                          "traffic_source": "ncu dram__bytes_read+write, 16x8192 capture, "
@@ -446,7 +462,8 @@ def run_batched_decode(args):
             "cpu_baseline": cpu,
             "e2e": {"value": NSEQ * K / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": K * LAYERS * (1 + kv.decode_kernel_count(n * hkv, HD, HQ // HKV)
+            "gpu_launches": K * LAYERS * ((1 if args.separate else 0)
+                                          + kv.decode_kernel_count(n * hkv, HD, HQ // HKV)
                                           + (1 if p2p else 0)),
             "clocks": clocks,
         }
@@ -474,7 +491,9 @@ def run_c1_32k(args, layers: int = 28, ctx: int = 32768, replays: int = 50):
     32768 and attended over 32,769 positions, for each of 28 layers.  The 28
     layers are captured in one CUDA graph and timed as replays with CUDA
     events; `decode_us_per_layer` is the decode call alone (q already
-    rotated), `step_us_per_layer` includes the fused RoPE + append.  The 28
+    rotated), `step_us_per_layer` adds the RoPE + append launch in front of
+    it, and `one_launch_step_us_per_layer` is the whole step as one
+    hx_append_decode_attention launch per layer.  The 28
     layers hold 1.88 GB of K/V, so no layer's 67 MB is still in L2 when it
     is read again."""
     import torch
@@ -501,18 +520,23 @@ def run_c1_32k(args, layers: int = 28, ctx: int = 32768, replays: int = 50):
     ws = torch.zeros(cache.workspace_bytes(1, hq), dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream()
 
-    def step(with_append):
+    def step(mode):
         for l in range(layers):
-            if with_append:
+            if mode == "one_launch":
+                cache.append_decode(l, q[l], k[l], v[l], sid, lens, hq, table=table, out=out[l],
+                                    workspace=ws, stream=stream)
+                continue
+            if mode == "step":
                 cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
                                   q_out=q_rot[l], stream=stream)
             cache.decode(l, q_rot[l], sid, lens, hq, out=out[l], workspace=ws, stream=stream)
 
     res = {}
     with torch.cuda.stream(stream):
-        step(True)  # kernel attributes are set outside the capture
+        step("step")  # kernel attributes are set outside the capture
+        step("one_launch")
         torch.cuda.synchronize()
-        for name, app in (("decode", False), ("step", True)):
+        for name, app in (("decode", "decode"), ("step", "step"), ("one_launch", "one_launch")):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 step(app)
@@ -536,11 +560,13 @@ def run_c1_32k(args, layers: int = 28, ctx: int = 32768, replays: int = 50):
     dec_gbs = dec_bytes / (res["decode"] * 1e-6) / 1e9
     return {"workload": "qwen2.5-7b attention, batch 1, 32769 positions, 28 layers, CUDA graph",
             "decode_us_per_layer": res["decode"], "step_us_per_layer": res["step"],
+            "one_launch_step_us_per_layer": res["one_launch"],
             "decode_bytes_per_layer": dec_bytes, "step_bytes_per_layer": step_bytes,
             "decode_gbs": dec_gbs, "frac_measured_peak": dec_gbs / peak, "peak_kind": peak_kind,
             "frac_8tbs": dec_gbs / 8000.0,
             "target_us_per_layer": dec_bytes / (0.75 * 8000e9) * 1e6,
             "step_gbs": step_bytes / (res["step"] * 1e-6) / 1e9,
+            "one_launch_step_gbs": step_bytes / (res["one_launch"] * 1e-6) / 1e9,
             "replays": replays, "launch": "programmatic dependent (HX_KV_OVERLAP_LAUNCH)"}
 
 
@@ -553,6 +579,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c1-32k", action="store_true",
                     help="skip the batch-1 Qwen 32k decode sub-record (N=1 only)")
+    ap.add_argument("--separate", action="store_true",
+                    help="K1 and K2 as two launches per layer (hx_rope_append then "
+                         "hx_decode_attention) instead of hx_append_decode_attention")
     ap.add_argument("--overlap", action="store_true",
                     help="launch append and decode as programmatic dependents (HX_KV_OVERLAP_LAUNCH)")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],

@@ -40,6 +40,11 @@ class hx_rope_config(C.Structure):
                 ("yarn_beta_slow", C.c_float), ("yarn_orig_max_pos", C.c_int32)]
 
 
+class hx_append_spec(C.Structure):
+    _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("bq", C.c_void_p), ("bk", C.c_void_p),
+                ("bv", C.c_void_p), ("dtype", C.c_int32), ("table", C.c_void_p)]
+
+
 _P = C.c_void_p
 _I = C.c_int
 # name -> (restype, argtypes); this table is the Python view of include/hx_kv.h
@@ -67,6 +72,8 @@ SIGNATURES = {
                                  C.c_size_t, _P]),
     "hx_decode_attention_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P, _I,
                                          _P]),
+    "hx_append_decode_attention": (_I, [_P, _I, _P, C.POINTER(hx_append_spec), _P, _P, _I, _I,
+                                        C.c_float, _P, _I, _P, C.c_size_t, _P]),
     "hx_prefill_attention": (_I, [_P, _I, _P, _I, _I, _I, _I, C.c_float, _P, _I, _P]),
     "hx_snapshot_bytes": (C.c_size_t, [_P, _I]),
     "hx_kv_snapshot": (_I, [_P, _I, _I, _P, C.c_size_t, _P]),
@@ -83,6 +90,9 @@ SIGNATURES = {
     "hx_dist_buffer": (_P, [_P]),
     "hx_decode_attention_gather": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, C.c_float, _P,
                                         C.c_size_t, _P, _I, _I, _I, _P, C.c_size_t, _P]),
+    "hx_append_decode_attention_gather": (_I, [_P, _I, _P, C.POINTER(hx_append_spec), _P, _P,
+                                               _I, _I, C.c_float, _P, C.c_size_t, _P, _I, _I,
+                                               _I, _P, C.c_size_t, _P]),
     "hx_dist_wait": (_I, [_P, C.c_uint32, _P]),
 }
 

@@ -88,6 +88,22 @@ struct DecodeParams {
     // that completes a segment's last piece merges its pieces itself and
     // returns the counter to zero; null = the separate combine kernel merges.
     unsigned int* fold_cnt;
+    // Append-and-decode (k_new != null): every sequence s brings one new
+    // token, at position lengths[s] - 1.  q is then its raw q rows (bias and
+    // RoPE still to apply) and k_new / v_new its raw K / V rows
+    // [n_seqs][hkv * 128], in q's dtype like the optional biases.  The CTA
+    // whose range holds a segment's newest tile writes the token's K and V
+    // row into the cache before loading that tile; every CTA applies the bias
+    // and the rotation to its q rows as it loads them.  The arithmetic is K1's,
+    // so cache and output equal hx_rope_append followed by
+    // hx_decode_attention bit for bit.
+    const void* k_new;
+    const void* v_new;
+    const void* bq;
+    const void* bk;
+    const void* bv;
+    const float2* rope;        // [rope_max_pos][64] (cos, sin), or null: no rotation
+    int rope_max_pos;
 };
 
 constexpr int kMinTilesPerCta = 2;  // small problems use fewer CTAs, hence fewer pieces
@@ -358,6 +374,82 @@ __device__ void fold_merge_rows(const DecodeParams& p, int seg, int n_seg, int c
     }
 }
 
+// Append-and-decode, producer warp: writes the new token of sequence slot s
+// (cache sequence seq) for kv head h at position pos into physical block pb,
+// with K1's bias rounding and rotation; lane l takes the pairs (l, l + 64) and
+// (l + 32, l + 96).
+template <typename T>
+__device__ void append_new_token(const DecodeParams& p, int s, int h, int pos, int64_t pb, int lane)
+{
+    const KVView& v = p.view;
+    const int64_t src = ((int64_t)s * v.hkv + h) * 128;
+    const T* k = static_cast<const T*>(p.k_new) + src;
+    const T* vv = static_cast<const T*>(p.v_new) + src;
+    const T* bk = p.bk ? static_cast<const T*>(p.bk) + (int64_t)h * 128 : nullptr;
+    const T* bv = p.bv ? static_cast<const T*>(p.bv) + (int64_t)h * 128 : nullptr;
+    const float2* cs = p.rope ? p.rope + (int64_t)pos * 64 : nullptr;
+    const int64_t off = pb * v.block_stride + (int64_t)h * v.head_stride + (int64_t)(pos % kBlockTokens) * 256;
+    __half* kd = reinterpret_cast<__half*>(v.k + off);
+    __half* vd = reinterpret_cast<__half*>(v.v + off);
+    // every load first (one round of latency), then the stores
+    float kx[4], vx[4];
+    float2 c2[2] = {make_float2(1.f, 0.f), make_float2(1.f, 0.f)};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int d = lane + 32 * u;  // u = 0, 1: x1 of pair lane + 32u; u = 2, 3: its x2
+        kx[u] = ld_bias(k + d, bk ? bk + d : nullptr);
+        vx[u] = ld_bias(vv + d, bv ? bv + d : nullptr);
+    }
+    if (cs) {
+        c2[0] = cs[lane];
+        c2[1] = cs[lane + 32];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) rotate(kx[u], kx[u + 2], c2[u], kx[u], kx[u + 2]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        kd[lane + 32 * u] = __float2half_rn(kx[u]);
+        vd[lane + 32 * u] = __float2half_rn(vx[u]);
+    }
+}
+
+// Append-and-decode, consumers: this lane's B-operand words of q row r of
+// the piece (q head qh of sequence slot s), with K1's bias and rotation.  The
+// lane holds dims 16kk + 2t4 + 8half (+1); the NeoX partner of a dim below 64
+// sits at kk + 4 of the same lane, so the rotation needs no exchange.
+template <typename T>
+__device__ __forceinline__ void load_q_new(const DecodeParams& p, int s, int qh, const float2* cs,
+                                           int t4, uint32_t (&qw)[8][2])
+{
+    const int64_t base = ((int64_t)s * p.hq + qh) * 128;
+    const T* q = static_cast<const T*>(p.q) + base;
+    const T* b = p.bq ? static_cast<const T*>(p.bq) + (int64_t)qh * 128 : nullptr;
+    float x[8][2][2];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int d = 16 * kk + 2 * t4 + 8 * half + e;
+                x[kk][half][e] = ld_bias(q + d, b ? b + d : nullptr);
+            }
+    if (cs) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+                for (int e = 0; e < 2; ++e)
+                    rotate(x[kk][half][e], x[kk + 4][half][e], cs[16 * kk + 2 * t4 + 8 * half + e],
+                           x[kk][half][e], x[kk + 4][half][e]);
+    }
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) qw[kk][half] = pack_half2(x[kk][half][0], x[kk][half][1]);
+}
+
 template <int ROWS, int STAGES, int CTAS_PER_SM>
 __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
     decode_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -433,6 +525,22 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
                 win_pb = phys_block(v, win_seq, win_j0 + lane);
             }
             const int64_t pb = __shfl_sync(0xffffffffu, win_pb, cur.j - win_j0);
+            if (p.k_new && cur.j == cur.tiles - 1) {
+                // append-and-decode: this CTA holds the segment's newest tile,
+                // so it writes the new token there before loading the tile
+                // the cursor's length is the sequence's unless the plan saw an
+                // empty or over-capacity one (then the raw length decides)
+                const int len = sc.odd_lengths ? p.lengths[cur.s] : cur.len;
+                const int pos = len - 1;
+                if (len >= 1 && len <= v.capacity && pb >= 0 && (!p.rope || pos < p.rope_max_pos)) {
+                    if (p.q_f32) append_new_token<float>(p, cur.s, cur.h, pos, pb, lane);
+                    else append_new_token<__half>(p, cur.s, cur.h, pos, pb, lane);
+                    fence_proxy_async_global();  // the writes before the tile's TMA load
+                } else if (lane == 0) {
+                    record_status(p.status, HX_ERR_CAPACITY);
+                }
+                __syncwarp();
+            }
             if (lane == 0) {
                 if (pb < 0) {
                     // unmapped block: no copy is issued; the consumers still get
@@ -493,26 +601,43 @@ __global__ void __launch_bounds__(kDecThreads, CTAS_PER_SM)
                 piece_whole = cta_of_tile(sm.cstart, n_eff, a) == cta_of_tile(sm.cstart, n_eff, b - 1);
             }
             const int64_t qrow0 = ((int64_t)cur.s * p.hq + (int64_t)cur.h * p.group) * 128;
+            const float2* q_cs = nullptr;  // append-and-decode: the new token's (cos, sin) row
+            if (p.k_new && p.rope) {
+                const int pos = cur.len - 1;  // as the producer's append (clamped lengths are an error)
+                if (pos >= 0 && pos < p.rope_max_pos) q_cs = p.rope + (int64_t)pos * 64;
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int r = 8 * nt + g;
+                if (p.k_new) {
+                    if (r < p.group) {
+                        const int qh = cur.h * p.group + r;
+                        if (p.q_f32) load_q_new<float>(p, cur.s, qh, q_cs, t4, qb[nt]);
+                        else load_q_new<__half>(p, cur.s, qh, q_cs, t4, qb[nt]);
+                    } else {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
+                        for (int kk = 0; kk < 8; ++kk) qb[nt][kk][0] = qb[nt][kk][1] = 0u;
+                    }
+                }
+                if (!p.k_new) {
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {  // dims 16kk+2t4 (+8)
-                        uint32_t val = 0;
-                        if (r < p.group) {
-                            const int64_t idx = qrow0 + (int64_t)r * 128 + 16 * kk + 2 * t4 + 8 * half;
-                            if (p.q_f32) {
-                                const float2 f = *reinterpret_cast<const float2*>(
-                                    static_cast<const float*>(p.q) + idx);
-                                val = pack_half2(f.x, f.y);
-                            } else {
-                                val = *reinterpret_cast<const uint32_t*>(
-                                    static_cast<const __half*>(p.q) + idx);
+                    for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {  // dims 16kk+2t4 (+8)
+                            uint32_t val = 0;
+                            if (r < p.group) {
+                                const int64_t idx = qrow0 + (int64_t)r * 128 + 16 * kk + 2 * t4 + 8 * half;
+                                if (p.q_f32) {
+                                    const float2 f = *reinterpret_cast<const float2*>(
+                                        static_cast<const float*>(p.q) + idx);
+                                    val = pack_half2(f.x, f.y);
+                                } else {
+                                    val = *reinterpret_cast<const uint32_t*>(
+                                        static_cast<const __half*>(p.q) + idx);
+                                }
                             }
+                            qb[nt][kk][half] = val;
                         }
-                        qb[nt][kk][half] = val;
                     }
                 }
 #pragma unroll
@@ -1154,17 +1279,43 @@ extern "C" int hx_decode_attention(const hx_kv_cache* c, int layer, const void* 
     return run_decode(c, p, workspace, (cudaStream_t)stream);
 }
 
-// Gathering decode: the rows go to every rank's buffer (the endpoints and
-// the epoch exchange live in dist.cu).
-extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const void* q,
-                                          int q_dtype, const int32_t* seq_ids,
-                                          const int32_t* lengths, int n_seqs, int num_q_heads,
-                                          float scale, hx_dist* dist, size_t out_offset,
-                                          const int32_t* out_rows, int out_row_heads,
-                                          int out_head0, int out_dtype, void* workspace,
-                                          size_t workspace_bytes, hx_stream_t stream)
+namespace hx {
+
+// Append-and-decode: checks the new-token inputs and puts them into p (whose
+// base fields are set).  Only the fast path fuses the append.
+static int append_params(const hx_kv_cache* c, const hx_append_spec* a, DecodeParams& p)
 {
-    HX_NVTX_RANGE("hx_decode_attention_gather");
+    if (!a) return fail(HX_ERR_INVALID, "null append spec");
+    if (p.n_seqs > 0 && (!a->k || !a->v)) return fail(HX_ERR_INVALID, "null k/v rows");
+    if (a->table) {
+        if (a->table->cfg.head_dim != c->cfg.head_dim)
+            return fail(HX_ERR_INVALID, "rope table head_dim %d != cache head_dim %d",
+                        a->table->cfg.head_dim, c->cfg.head_dim);
+        if (int rc = check_device(a->table->device, "the rope table")) return rc;
+    }
+    if (!fast_path(c, p))
+        return fail(HX_ERR_UNSUPPORTED,
+                    "append-and-decode needs head_dim 128 and at most 16 q heads per kv head "
+                    "(hx_rope_append then hx_decode_attention cover the rest)");
+    p.k_new = a->k;
+    p.v_new = a->v;
+    p.bq = a->bq;
+    p.bk = a->bk;
+    p.bv = a->bv;
+    p.rope = a->table ? a->table->d_cos_sin : nullptr;
+    p.rope_max_pos = a->table ? a->table->cfg.max_pos : 0;
+    return HX_OK;
+}
+
+// Gathering decode, plain or with the new tokens' append (a != null): the
+// rows go to every rank's buffer (the endpoints and the epoch exchange live
+// in dist.cu).
+static int decode_gather(const hx_kv_cache* c, int layer, const void* q, int q_dtype,
+                         const hx_append_spec* a, const int32_t* seq_ids, const int32_t* lengths,
+                         int n_seqs, int num_q_heads, float scale, hx_dist* dist, size_t out_offset,
+                         const int32_t* out_rows, int out_row_heads, int out_head0, int out_dtype,
+                         void* workspace, size_t workspace_bytes, hx_stream_t stream)
+{
     if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
                                  out_dtype))
         return rc;
@@ -1201,12 +1352,71 @@ extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const
     p.out_row_limit = rows > (size_t)INT32_MAX ? INT32_MAX : (int)rows;
     p.status = status_word();
     cudaStream_t s = (cudaStream_t)stream;
+    if (a)
+        if (int rc = append_params(c, a, p)) return rc;
     if (n_seqs == 0) return HX_OK;
     const size_t need = needed_scratch(c, p);
     if (need && (!workspace || workspace_bytes < need))
         return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
                     workspace_bytes, need);
     return run_decode(c, p, workspace, s);
+}
+
+}  // namespace hx
+
+extern "C" int hx_decode_attention_gather(const hx_kv_cache* c, int layer, const void* q,
+                                          int q_dtype, const int32_t* seq_ids,
+                                          const int32_t* lengths, int n_seqs, int num_q_heads,
+                                          float scale, hx_dist* dist, size_t out_offset,
+                                          const int32_t* out_rows, int out_row_heads,
+                                          int out_head0, int out_dtype, void* workspace,
+                                          size_t workspace_bytes, hx_stream_t stream)
+{
+    HX_NVTX_RANGE("hx_decode_attention_gather");
+    return decode_gather(c, layer, q, q_dtype, nullptr, seq_ids, lengths, n_seqs, num_q_heads,
+                         scale, dist, out_offset, out_rows, out_row_heads, out_head0, out_dtype,
+                         workspace, workspace_bytes, stream);
+}
+
+extern "C" int hx_append_decode_attention(hx_kv_cache* c, int layer, const void* q,
+                                          const hx_append_spec* append, const int32_t* seq_ids,
+                                          const int32_t* lengths, int n_seqs, int num_q_heads,
+                                          float scale, void* out, int out_dtype, void* workspace,
+                                          size_t workspace_bytes, hx_stream_t stream)
+{
+    HX_NVTX_RANGE("hx_append_decode_attention");
+    const int q_dtype = append ? append->dtype : HX_FP16;
+    if (int rc = validate_decode(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 out_dtype))
+        return rc;
+    if (n_seqs > 0 && !out) return fail(HX_ERR_INVALID, "null out");
+    DecodeParams p = base_params(c, layer, q, q_dtype, seq_ids, lengths, n_seqs, num_q_heads,
+                                 scale, out_dtype);
+    if (int rc = append_params(c, append, p)) return rc;
+    if (n_seqs == 0) return HX_OK;
+    p.out = out;
+    p.outs[0] = out;
+    p.n_outs = 1;
+    p.out_vec = reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    p.status = status_word();
+    const size_t need = needed_scratch(c, p);
+    if (need && (!workspace || workspace_bytes < need))
+        return fail(HX_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu needed",
+                    workspace_bytes, need);
+    return run_decode(c, p, workspace, (cudaStream_t)stream);
+}
+
+extern "C" int hx_append_decode_attention_gather(
+    hx_kv_cache* c, int layer, const void* q, const hx_append_spec* append, const int32_t* seq_ids,
+    const int32_t* lengths, int n_seqs, int num_q_heads, float scale, hx_dist* dist,
+    size_t out_offset, const int32_t* out_rows, int out_row_heads, int out_head0, int out_dtype,
+    void* workspace, size_t workspace_bytes, hx_stream_t stream)
+{
+    HX_NVTX_RANGE("hx_append_decode_attention_gather");
+    if (!append) return fail(HX_ERR_INVALID, "null append spec");
+    return decode_gather(c, layer, q, append->dtype, append, seq_ids, lengths, n_seqs, num_q_heads,
+                         scale, dist, out_offset, out_rows, out_row_heads, out_head0, out_dtype,
+                         workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- no-allocation variant

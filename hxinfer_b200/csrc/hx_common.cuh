@@ -102,6 +102,13 @@ __device__ __forceinline__ void fence_proxy_async_smem()
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's earlier generic-proxy global writes before later
+// async-proxy (TMA) reads of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy()
 {
     uint64_t policy;
@@ -173,6 +180,51 @@ __device__ __forceinline__ float fast_exp2(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ---- K1 numerics (rope_append.cu and the append-and-decode path) ----
+// The bias add rounds like the reference (fp16 __hadd, bias_add.cu:6-11, or
+// an fp32 add); the NeoX rotation of a pair (x1, x2) = (x[d], x[d + hd/2])
+// evaluates x1*c - x2*s and x2*c + x1*s with separately rounded multiplies
+// and adds, the order of rope_cpu.cpp:29-30 without FMA contraction.
+template <typename T>
+__device__ __forceinline__ float ld(const T* p)
+{
+    return (float)*p;
+}
+template <>
+__device__ __forceinline__ float ld<__half>(const __half* p)
+{
+    return __half2float(*p);
+}
+
+// x + b with the reference's rounding: fp16 __hadd (bias_add.cu:6-11) or fp32 add.
+template <typename T>
+__device__ __forceinline__ float ld_bias(const T* x, const T* b)
+{
+    return b ? __fadd_rn(*x, *b) : (float)*x;
+}
+template <>
+__device__ __forceinline__ float ld_bias<__half>(const __half* x, const __half* b)
+{
+    return b ? __half2float(__hadd(*x, *b)) : __half2float(*x);
+}
+
+template <typename T>
+__device__ __forceinline__ void st(T* p, float v)
+{
+    *p = v;
+}
+template <>
+__device__ __forceinline__ void st<__half>(__half* p, float v)
+{
+    *p = __float2half_rn(v);
+}
+
+__device__ __forceinline__ void rotate(float x1, float x2, float2 cs, float& o1, float& o2)
+{
+    o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+    o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)

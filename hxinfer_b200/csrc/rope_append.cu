@@ -15,45 +15,8 @@
 
 namespace hx {
 
-template <typename T>
-__device__ __forceinline__ float ld(const T* p)
-{
-    return (float)*p;
-}
-template <>
-__device__ __forceinline__ float ld<__half>(const __half* p)
-{
-    return __half2float(*p);
-}
-
-// x + b with the reference's rounding: fp16 __hadd (bias_add.cu:6-11) or fp32 add.
-template <typename T>
-__device__ __forceinline__ float ld_bias(const T* x, const T* b)
-{
-    return b ? __fadd_rn(*x, *b) : (float)*x;
-}
-template <>
-__device__ __forceinline__ float ld_bias<__half>(const __half* x, const __half* b)
-{
-    return b ? __half2float(__hadd(*x, *b)) : __half2float(*x);
-}
-
-template <typename T>
-__device__ __forceinline__ void st(T* p, float v)
-{
-    *p = v;
-}
-template <>
-__device__ __forceinline__ void st<__half>(__half* p, float v)
-{
-    *p = __float2half_rn(v);
-}
-
-__device__ __forceinline__ void rotate(float x1, float x2, float2 cs, float& o1, float& o2)
-{
-    o1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-    o2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-}
+// ld / ld_bias / st / rotate (the K1 numerics) live in hx_common.cuh, shared
+// with the append-and-decode kernel.
 
 // grid (token, head group): each CTA takes heads_per_cta consecutive head
 // slots of one token, one thread per NeoX pair (d, d + head_dim/2), so every

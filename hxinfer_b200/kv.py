@@ -247,6 +247,36 @@ class KVCache:
                                          _stream(stream)), "decode attention")
         return out
 
+    def _append_spec(self, k, v, bq, bk, bv, table):
+        return _lib.hx_append_spec(k=_ptr(k), v=_ptr(v), bq=_ptr(bq), bk=_ptr(bk), bv=_ptr(bv),
+                                   dtype=_dt(k), table=table.handle if table else None)
+
+    def append_decode(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      seq_ids: torch.Tensor, lengths: torch.Tensor, num_q_heads: int, *,
+                      table: "RopeTable | None" = None, bq=None, bk=None, bv=None,
+                      scale: float | None = None, out: torch.Tensor | None = None,
+                      out_dtype=torch.float16, workspace: torch.Tensor | None = None,
+                      stream=None):
+        """One decode step in one launch (hx_append_decode_attention): every
+        sequence's raw q / k / v rows of the token at position lengths - 1 get
+        the bias and RoPE, K / V go into the cache, then attention over
+        `lengths` positions.  Equal to rope_append + decode."""
+        _need_cuda(q, k, v, seq_ids, lengths, out, workspace, bq, bk, bv)
+        n = seq_ids.numel()
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            out = torch.empty((n, num_q_heads * self.head_dim), dtype=out_dtype, device=q.device)
+        if workspace is None:
+            workspace = torch.zeros(max(self.workspace_bytes(n, num_q_heads), 16),
+                                    dtype=torch.uint8, device=q.device)
+        spec = self._append_spec(k, v, bq, bk, bv, table)
+        check(load().hx_append_decode_attention(
+            self.handle, layer, _ptr(q), C.byref(spec), _ptr(seq_ids), _ptr(lengths), n,
+            num_q_heads, scale, _ptr(out), _dt(out), _ptr(workspace),
+            workspace.numel() * workspace.element_size(), _stream(stream)), "append decode")
+        return out
+
     def decode_gather(self, layer: int, q: torch.Tensor, seq_ids: torch.Tensor,
                       lengths: torch.Tensor, num_q_heads: int, gather: "PeerGather", *,
                       out_offset: int, out_rows: torch.Tensor, out_row_heads: int,
@@ -272,6 +302,30 @@ class KVCache:
             scale, gather.handle, out_offset, _ptr(out_rows), out_row_heads, out_head0, odt,
             _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
             "decode attention (gather)")
+
+    def append_decode_gather(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                             seq_ids: torch.Tensor, lengths: torch.Tensor, num_q_heads: int,
+                             gather: "PeerGather", *, out_offset: int, out_rows: torch.Tensor,
+                             out_row_heads: int, out_head0: int, table: "RopeTable | None" = None,
+                             bq=None, bk=None, bv=None, scale: float | None = None,
+                             out_dtype=torch.float16, workspace: torch.Tensor | None = None,
+                             stream=None):
+        """append_decode with the outputs placed as decode_gather places them
+        (hx_append_decode_attention_gather)."""
+        _need_cuda(q, k, v, seq_ids, lengths, out_rows, workspace, bq, bk, bv)
+        n = seq_ids.numel()
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if workspace is None:
+            workspace = torch.zeros(max(self.workspace_bytes(n, num_q_heads), 16),
+                                    dtype=torch.uint8, device=q.device)
+        odt = HX_FP32 if out_dtype == torch.float32 else HX_FP16
+        spec = self._append_spec(k, v, bq, bk, bv, table)
+        check(load().hx_append_decode_attention_gather(
+            self.handle, layer, _ptr(q), C.byref(spec), _ptr(seq_ids), _ptr(lengths), n,
+            num_q_heads, scale, gather.handle, out_offset, _ptr(out_rows), out_row_heads,
+            out_head0, odt, _ptr(workspace), workspace.numel() * workspace.element_size(),
+            _stream(stream)), "append decode (gather)")
 
     def prefill(self, layer: int, q: torch.Tensor, seq: int, start: int, num_q_heads: int, *,
                 scale: float | None = None, out: torch.Tensor | None = None,

@@ -226,6 +226,38 @@ int hx_decode_attention(const hx_kv_cache* cache, int layer, const void* q, int 
                         int num_q_heads, float scale, void* out, int out_dtype, void* workspace,
                         size_t workspace_bytes, hx_stream_t stream);
 
+/* The new token of every sequence of an append-and-decode call (one token
+ * per sequence, at position lengths[s] - 1): its raw K and V rows and the
+ * optional biases, all in `dtype` (HX_FP16 or HX_FP32, also the dtype of q),
+ * and the optional RoPE table (NULL: no rotation). */
+typedef struct {
+    const void* k;                 /* device [n_seqs][num_kv_heads*head_dim] */
+    const void* v;                 /* device [n_seqs][num_kv_heads*head_dim] */
+    const void* bq;                /* [num_q_heads*head_dim] or NULL */
+    const void* bk;                /* [num_kv_heads*head_dim] or NULL */
+    const void* bv;                /* [num_kv_heads*head_dim] or NULL */
+    int32_t dtype;
+    const hx_rope_table* table;
+} hx_append_spec;
+
+/* K1 + K2 in one launch: for every sequence, the bias and RoPE of q and k,
+ * the append of the token's K/V row at position lengths[s] - 1, then decode
+ * attention over lengths[s] positions.  Replaces the reference's
+ * attention_score_cuda (attention_score_cuda.cu:163-214), which appends
+ * curr_k / curr_v and attends in one host call, together with the bias adds
+ * and rope_cuda in front of it (attention.cpp:21-35).  q: the raw q rows
+ * [n_seqs][num_q_heads*head_dim] in append->dtype.  Equal bit for bit, in
+ * the cache and in out, to hx_rope_append (positions lengths - 1, q_out
+ * fp16) followed by hx_decode_attention; the cache must be as hx_decode_
+ * attention needs it (head_dim 128, at most 16 q heads per kv head; else
+ * HX_ERR_UNSUPPORTED).  The workspace is hx_decode_workspace_bytes, with its
+ * rules. */
+int hx_append_decode_attention(hx_kv_cache* cache, int layer, const void* q,
+                               const hx_append_spec* append, const int32_t* seq_ids,
+                               const int32_t* lengths, int n_seqs, int num_q_heads, float scale,
+                               void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                               hx_stream_t stream);
+
 /* K3: causal prefill attention on the tcgen05 tensor cores.  Query rows
  * i in [0, n) sit at positions start + i of sequence `seq` and attend to
  * positions [0, start + i] of the cache (their own K/V must already be
@@ -311,6 +343,15 @@ int hx_decode_attention_gather(const hx_kv_cache* cache, int layer, const void* 
                                const int32_t* out_rows, int out_row_heads, int out_head0,
                                int out_dtype, void* workspace, size_t workspace_bytes,
                                hx_stream_t stream);
+/* hx_append_decode_attention with the outputs placed as
+ * hx_decode_attention_gather places them. */
+int hx_append_decode_attention_gather(hx_kv_cache* cache, int layer, const void* q,
+                                      const hx_append_spec* append, const int32_t* seq_ids,
+                                      const int32_t* lengths, int n_seqs, int num_q_heads,
+                                      float scale, hx_dist* dist, size_t out_offset,
+                                      const int32_t* out_rows, int out_row_heads, int out_head0,
+                                      int out_dtype, void* workspace, size_t workspace_bytes,
+                                      hx_stream_t stream);
 /* Exchanges `epoch` with every other rank: once everything launched before
  * it on `stream` has completed, posts `epoch` to every other rank and holds
  * the stream until every other rank has posted it here (one warp; rows a

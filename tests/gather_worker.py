@@ -13,6 +13,10 @@ Checks on every rank:
     attention tolerance (max abs 2e-3, max rel 1e-2 of the output scale).
 The cases cover sequence and kv-head sharding, a rank without sequences, fp32
 output and a call with enough segments for the two-CTAs-per-SM decode shape.
+Then, for the same cases, the one-launch step (hx_append_decode_attention_
+gather: bias-free RoPE + append of each sequence's newest token, then the
+gathering decode) is checked bit for bit against hx_rope_append followed by
+hx_decode_attention_gather on a second copy of the shard.
 Then rank 0 waits for an epoch that no rank posts: the bounded device wait
 must end with HX_ERR_TIMEOUT in the status word and leave the context usable.
 Prints "RANK <r> OK" at the end.
@@ -137,6 +141,72 @@ def run_case(rank, world, dev, name, hq, hkv, lengths, out_dtype):
     return epoch
 
 
+def run_fused_case(rank, world, dev, name, hq, hkv, lengths, out_dtype, epoch):
+    """The newest position of every sequence arrives as raw q / k / v rows:
+    append_decode_gather on one copy of the shard against rope_append +
+    decode_gather on another; both gathered buffers must be equal."""
+    n_all = len(lengths)
+    group = hq // hkv
+    mode, shards = hxdist.plan(world, hkv, lengths)
+    seqs, heads = shards[rank]
+    n = len(seqs)
+    cap = max(lengths) + 1
+    g = torch.Generator().manual_seed(4321 + n_all)
+    K = [torch.randn((L, hkv * HD), generator=g).half() for L in lengths]
+    V = [torch.randn((L, hkv * HD), generator=g).half() for L in lengths]
+    Q = torch.randn((n_all, hq * HD), generator=g).half()
+
+    def cols(t, hs, width):
+        return torch.cat([t[..., h * width:(h + 1) * width] for h in hs], dim=-1)
+
+    caches = [kv.KVCache(1, len(heads), HD, max(n, 1), cap) for _ in range(2)]
+    for c in caches:
+        for i, s in enumerate(seqs):
+            c.reserve(i, lengths[s])
+            if lengths[s] > 1:  # history; the newest position comes with the step
+                c.write(0, i, 0, cols(K[s][:-1], heads, HD).contiguous().to(dev),
+                        cols(V[s][:-1], heads, HD).contiguous().to(dev))
+    qh = [h * group + j for h in heads for j in range(group)]
+    q_loc = cols(Q[seqs], qh, HD).contiguous().to(dev) if n else \
+        torch.empty((0, len(qh) * HD), dtype=torch.float16, device=dev)
+    k_new = cols(torch.stack([K[s][-1] for s in seqs]), heads, HD).contiguous().to(dev) if n else \
+        torch.empty((0, len(heads) * HD), dtype=torch.float16, device=dev)
+    v_new = cols(torch.stack([V[s][-1] for s in seqs]), heads, HD).contiguous().to(dev) if n else \
+        torch.empty((0, len(heads) * HD), dtype=torch.float16, device=dev)
+    table = kv.RopeTable(HD, cap, 1e6)
+    sid = torch.arange(n, dtype=torch.int32, device=dev)
+    lens = torch.tensor([lengths[s] for s in seqs], dtype=torch.int32, device=dev)
+    rows = torch.tensor(seqs, dtype=torch.int32, device=dev)
+    esize = 4 if out_dtype == torch.float32 else 2
+    layer_bytes = n_all * hq * HD * esize
+    peer = kv.PeerGather(rank, world, 2 * layer_bytes, exchange_fn(world))
+    place = dict(out_rows=rows, out_row_heads=hq, out_head0=heads[0] * group, out_dtype=out_dtype)
+    q_rot = torch.empty_like(q_loc)
+    if n:
+        caches[0].rope_append(0, k_new, v_new, sid, lens - 1, q=q_loc, num_q_heads=len(qh),
+                              table=table, q_out=q_rot)
+    epoch += 1
+    caches[0].decode_gather(0, q_rot, sid, lens, len(qh), peer, out_offset=0, **place)
+    peer.wait(epoch)
+    epoch += 1
+    caches[1].append_decode_gather(0, q_loc, k_new, v_new, sid, lens, len(qh), peer,
+                                   out_offset=layer_bytes, table=table, **place)
+    peer.wait(epoch)
+    kv.device_status()
+    got = peer.view(out_dtype, shape=(2, n_all, hq * HD)).cpu()
+    if not torch.equal(got[0], got[1]):
+        bad = (got[0] != got[1]).nonzero()
+        raise AssertionError(f"{name}: one-launch step differs from append + decode at "
+                             f"{bad[:5].tolist()} ({len(bad)} elements)")
+    torch.cuda.synchronize()
+    dist.barrier()
+    peer.close()
+    table.close()
+    for c in caches:
+        c.close()
+    return epoch
+
+
 def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -144,8 +214,13 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("gloo", timeout=timedelta(seconds=90))
+    epoch = 0
     for case in CASES:
-        run_case(rank, world, dev, *case)
+        epoch = run_case(rank, world, dev, *case)
+        dist.barrier()
+    epoch = 10000
+    for case in CASES:
+        epoch = run_fused_case(rank, world, dev, *case, epoch)
         dist.barrier()
 
     # bounded wait that runs out: nobody posts this epoch

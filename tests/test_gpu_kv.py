@@ -630,3 +630,63 @@ def test_block_allocator_release_and_reuse(hx):
     from hxinfer_b200._lib import HXError
     with pytest.raises(HXError):
         cache.reserve(1, 257)
+
+
+# ------------------------------------------------------------------ K1 + K2 in one launch
+
+@pytest.mark.parametrize("name,Hq,Hkv,lens,dtype,bias,rope", [
+    ("qwen_batch1_32k", 28, 4, [32769], torch.float16, True, True),
+    ("qwen_block_start", 28, 4, [1025, 65, 64, 1], torch.float16, True, True),
+    ("llama3_wide_folded", 32, 8, None, torch.float16, False, True),
+    ("group16_fp32", 32, 2, [2000, 33, 129], torch.float32, True, True),
+    ("mha_no_rope", 8, 8, [300, 7], torch.float16, False, False),
+])
+def test_append_decode_equals_append_then_decode(hx, name, Hq, Hkv, lens, dtype, bias, rope):
+    """hx_append_decode_attention (bias + RoPE + append + decode in one
+    launch) against hx_rope_append at positions lengths - 1 followed by
+    hx_decode_attention on a copy of the same cache: the appended cache rows
+    and the outputs are equal bit for bit, on two steps in a row."""
+    if lens is None:
+        lens = [int(x) for x in np.random.default_rng(3).integers(1, 3000, 64)]
+    n, hd = len(lens), 128
+    cap = max(lens) + 2
+    caches = [make_cache(hx, 2, Hkv, n, cap) for _ in range(2)]
+    for c in caches:
+        for s in range(n):
+            c.reserve(s, cap)
+        c.fill_normal(99)
+    table = hx.RopeTable(hd, cap, 1e6) if rope else None
+    g = torch.Generator(device="cuda").manual_seed(len(lens))
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
+    for step in range(2):
+        lengths = torch.tensor(lens, dtype=torch.int32, device="cuda") + step
+        q = torch.randn((n, Hq * hd), generator=g, device="cuda").to(dtype)
+        k = torch.randn((n, Hkv * hd), generator=g, device="cuda").to(dtype)
+        v = torch.randn((n, Hkv * hd), generator=g, device="cuda").to(dtype)
+        bq, bk, bv = ((torch.randn((m * hd,), generator=g, device="cuda") * 0.1).to(dtype)
+                      for m in (Hq, Hkv, Hkv)) if bias else (None, None, None)
+        q_rot = torch.empty((n, Hq * hd), dtype=torch.float16, device="cuda")
+        caches[0].rope_append(1, k, v, sid, lengths - 1, q=q, num_q_heads=Hq, table=table,
+                              bq=bq, bk=bk, bv=bv, q_out=q_rot)
+        want = caches[0].decode(1, q_rot, sid, lengths, Hq)
+        got = caches[1].append_decode(1, q, k, v, sid, lengths, Hq, table=table, bq=bq, bk=bk, bv=bv)
+        torch.cuda.synchronize()
+        hx.device_status()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), f"{name} step {step}"
+        for s in range(n):
+            p0 = lens[s] + step - 1
+            k0, v0 = caches[0].read(1, s, p0, 1)
+            k1, v1 = caches[1].read(1, s, p0, 1)
+            assert torch.equal(k0.view(torch.int16), k1.view(torch.int16)), f"{name} K row {s}"
+            assert torch.equal(v0.view(torch.int16), v1.view(torch.int16)), f"{name} V row {s}"
+
+
+def test_append_decode_refuses_other_head_sizes(hx):
+    from hxinfer_b200._lib import HXError
+    cache = make_cache(hx, 1, 2, 1, 128, hd=64)
+    cache.reserve(0, 128)
+    q = torch.zeros((1, 4 * 64), dtype=torch.float16, device="cuda")
+    k = torch.zeros((1, 2 * 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(HXError):
+        cache.append_decode(0, q, k, k.clone(), torch.zeros(1, dtype=torch.int32, device="cuda"),
+                            torch.ones(1, dtype=torch.int32, device="cuda"), 4)
