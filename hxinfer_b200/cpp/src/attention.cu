@@ -188,6 +188,24 @@ void AttentionLayer::forward(std::shared_ptr<Tensor>& input, std::shared_ptr<Ten
                                 has_bias_ ? bk_->raw_data_ptr() : nullptr,
                                 has_bias_ ? bv_->raw_data_ptr() : nullptr, r, r + pos, 1,
                                 config_.head, table, q_rot_->raw_data_ptr(), at, nullptr);
+    } else if (head_dim == 128 && config_.kv_head > 0 && config_.head / config_.kv_head <= 16) {
+        // other weight dtypes: cuBLAS projections as the reference, then bias
+        // + RoPE + append + attention in one launch
+        project(wq_, input, curr_q_);
+        project(wk_, input, curr_k_);
+        project(wv_, input, curr_v_);
+        const hx_append_spec a{curr_k_->raw_data_ptr(), curr_v_->raw_data_ptr(),
+                               has_bias_ ? bq_->raw_data_ptr() : nullptr,
+                               has_bias_ ? bk_->raw_data_ptr() : nullptr,
+                               has_bias_ ? bv_->raw_data_ptr() : nullptr, at, table};
+        const size_t ws_bytes = hx_decode_workspace_bytes(kv_, 1, config_.head);
+        void* ws = detail::workspace(ws_bytes);
+        rc = hx_append_decode_attention(kv_, 0, curr_q_->raw_data_ptr(), &a, r, r + pos + 1, 1,
+                                        config_.head, 1.0f / sqrtf(static_cast<float>(head_dim)),
+                                        after_qktv_->raw_data_ptr(), at, ws, ws_bytes, nullptr);
+        if (rc != HX_OK) throw std::runtime_error(std::string("AttentionLayer: ") + hx_last_error());
+        project(wo_, after_qktv_, output);
+        return;
     } else {
         project(wq_, input, curr_q_);
         project(wk_, input, curr_k_);

@@ -91,14 +91,27 @@ void attention_score_cuda(const std::shared_ptr<Tensor>& q, const std::shared_pt
         std::cerr << "[hxinfer] attention_score_cuda: " << hx_last_error() << std::endl;
         return;
     }
+    const size_t ws_bytes = hx_decode_workspace_bytes(kv, 1, head);
+    const float scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    const int q_dt = hx_dtype_of(q->tensor_data_type()), k_dt = hx_dtype_of(curr_k->tensor_data_type());
+    if (head_dim == 128 && q_dt == k_dt && head / kv_head <= 16) {
+        // the append and the attention in one launch (q and k already
+        // rotated by rope_tensor: no table, no bias)
+        const hx_append_spec a{curr_k->raw_data_ptr(), curr_v->raw_data_ptr(), nullptr, nullptr,
+                               nullptr, k_dt, nullptr};
+        const int rc = hx_append_decode_attention(kv, 0, q->raw_data_ptr(), &a, r, r + pos + 1, 1,
+                                                  head, scale, output->raw_data_ptr(),
+                                                  hx_dtype_of(output->tensor_data_type()),
+                                                  detail::workspace(ws_bytes), ws_bytes, nullptr);
+        if (rc != HX_OK) std::cerr << "[hxinfer] attention_score_cuda: " << hx_last_error() << std::endl;
+        return;
+    }
     // append (the caller already rotated q and k with rope_tensor)
     int rc = hx_rope_append(kv, 0, nullptr, curr_k->raw_data_ptr(), curr_v->raw_data_ptr(),
                             hx_dtype_of(curr_k->tensor_data_type()), nullptr, nullptr, nullptr, r,
                             r + pos, 1, head, nullptr, nullptr, HX_FP16, nullptr);
     if (rc == HX_OK) {
-        const size_t ws_bytes = hx_decode_workspace_bytes(kv, 1, head);
         void* ws = detail::workspace(ws_bytes);
-        const float scale = 1.0f / sqrtf(static_cast<float>(head_dim));
         rc = hx_decode_attention(kv, 0, q->raw_data_ptr(), hx_dtype_of(q->tensor_data_type()), r,
                                  r + pos + 1, 1, head, scale, output->raw_data_ptr(),
                                  hx_dtype_of(output->tensor_data_type()), ws, ws_bytes, nullptr);
