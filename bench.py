@@ -11,7 +11,7 @@ aggregate decode tok/s; the decode kernel's achieved HBM GB/s is in
 ``roofline``.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--collective p2p|nccl] [--separate] [--overlap] [--no-cpu-baseline]
+                  [--collective p2p|nccl] [--separate] [--no-overlap] [--no-cpu-baseline]
                   [--no-c1-32k]
 
 At N=1 the same JSON line also carries ``c1_32k``: batch-1 decode on the
@@ -446,7 +446,11 @@ def run_batched_decode(args):
                        "parallelism": f"{mode}x{world}",
                        "collective": ("p2p gather fused into the decode kernels" if p2p else
                                       "nccl all_gather_into_tensor" if world > 1 else "none"),
-                       "l2": "inputs larger than L2 (KV cache >> 126 MB)"},
+                       "l2": "inputs larger than L2 (KV cache >> 126 MB)",
+                       "step": ("K1 then K2, two launches per layer" if args.separate else
+                                "RoPE + append + decode in one launch per layer"),
+                       "launch": ("programmatic dependent (HX_KV_OVERLAP_LAUNCH)" if args.overlap
+                                  else "stream-ordered")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": ("decode_attention_kernel (+ decode_combine_kernel when not "
@@ -582,8 +586,11 @@ def main():
     ap.add_argument("--separate", action="store_true",
                     help="K1 and K2 as two launches per layer (hx_rope_append then "
                          "hx_decode_attention) instead of hx_append_decode_attention")
-    ap.add_argument("--overlap", action="store_true",
-                    help="launch append and decode as programmatic dependents (HX_KV_OVERLAP_LAUNCH)")
+    ap.add_argument("--overlap", dest="overlap", action="store_true", default=True,
+                    help="launch the decode kernels as programmatic dependents "
+                         "(HX_KV_OVERLAP_LAUNCH; the default)")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="plain stream-ordered launches")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: gather fused into the decode kernels over NVLink peer memory "
                          "(p2p) or an NCCL all-gather after each decode call (nccl)")
