@@ -8,31 +8,38 @@
 //     out[i] = softmax(q_i . K[0 .. start+i]^T * scale) V
 // over the paged cache (the rows' own K/V must already be appended).
 //
-// One CTA per (128-row query tile, q head); 192 threads:
-//   warp 4  TMA producers: lane 0 the Q tile once (2 boxes 128x64, 128-byte
+// One CTA per (128-row query tile, q head); 320 threads:
+//   warp 8  TMA producers: lane 0 the Q tile once (2 boxes 128x64, 128-byte
 //           swizzle) then a 3-stage ring of 128-position K tiles (two cache
 //           blocks each); lane 1 a 3-stage ring of V tiles; block-table rows
 //           are read one tile ahead; no multicast.
-//   warp 5  TMEM allocator (512 columns) and, lane 0, the MMA issuer:
+//   warp 9  TMEM allocator (512 columns) and, lane 0, the MMA issuer:
 //           S_j = Q K_j^T  (M=128, N=128, K=16 x 8, fp16 -> fp32) into TMEM
-//           buffer j & 1, then O += P_j V_j with P_j read from that same
-//           buffer (V as an MN-major operand); order S_0, S_1, then PV_j,
-//           S_{j+2} for each j, so S_{j+1} runs during softmax j and S_{j+2}
-//           overwrites P_j only after PV_j (this thread's MMAs execute in
-//           order); completion via tcgen05.commit.
-//   warps 0-3  softmax: thread t owns query row t; reads S_j with tcgen05.ld,
-//           applies the causal mask, keeps a running max that only moves when
-//           it rises by more than 2^8 (then O in TMEM is rescaled), writes
-//           P_j = 2^(s - m) as fp16 over S_j's own columns with tcgen05.st,
-//           and in the end divides O by the row sum, staged through an idle
-//           K stage for coalesced stores.
+//           buffer j & 1, then for each key half w: O_w += P_j[:, w] V_j[w]
+//           (K = 16 x 4, P read from the S buffer, V as an MN-major
+//           operand, O_0 and O_1 in columns 256 and 384); order S_0, S_1,
+//           then PV_j (both halves), S_{j+2} for each j, so S_{j+1} runs
+//           during softmax j and S_{j+2} overwrites P_j only after PV_j (this
+//           thread's MMAs execute in order); completion via tcgen05.commit.
+//   warps 0-7  softmax in two warpgroups: warpgroup w takes key columns
+//           64 w .. 64 w + 63 of every tile, thread t (mod 128) query row t;
+//           reads its S columns with tcgen05.ld, applies the causal mask,
+//           keeps its own running max (moved only when it rises by more than
+//           2^8, then O_w is rescaled) and sum, and writes its P half as fp16
+//           over its own S columns with tcgen05.st.  The halves never wait
+//           for each other; the epilogue combines
+//           O = (a_0 O_0 + a_1 O_1) / (a_0 l_0 + a_1 l_1), staged through an
+//           idle K stage for coalesced stores.
 // Key tiles above the diagonal are never loaded.  Every mbarrier wait is
 // bounded; TMEM is always released before exit.
 #include "hx_common.cuh"
 
 namespace hx {
 
-constexpr int kPfThreads = 192;
+constexpr int kPfSoftmaxWarps = 8;             // two warpgroups: key halves of every tile
+constexpr int kPfProducerWarp = kPfSoftmaxWarps;  // TMA
+constexpr int kPfMmaWarp = kPfSoftmaxWarps + 1;   // TMEM allocation and the MMA issuer
+constexpr int kPfThreads = 32 * (kPfSoftmaxWarps + 2);
 constexpr int kRegionBytes = 128 * 128;  // 128 rows x 64 fp16 (one 128-byte swizzled region)
 constexpr int kPfKStages = 3, kPfVStages = 3;  // K and V tile rings
 
@@ -52,7 +59,8 @@ struct PrefillSmem {
     uint64_t q_full;
     uint64_t k_full[kPfKStages], k_empty[kPfKStages];
     uint64_t v_full[kPfVStages], v_empty[kPfVStages];
-    uint64_t s_full[2], p_full[2], pv_done[2];  // per TMEM S/P buffer
+    uint64_t s_full[2];                        // per TMEM S/P buffer
+    uint64_t p_full[2][2], pv_done[2][2];      // [key half][TMEM S/P buffer]
     uint64_t mma_idle;
     uint32_t tmem_base;
     int abort_flag;
@@ -212,14 +220,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.s_full[i], 1);
-            mbar_init(&sm.p_full[i], 4);
-            mbar_init(&sm.pv_done[i], 1);
+            for (int w = 0; w < 2; ++w) {
+                mbar_init(&sm.p_full[w][i], 4);  // the four warps of warpgroup w
+                mbar_init(&sm.pv_done[w][i], 1);
+            }
         }
         mbar_init(&sm.mma_idle, 1);
         sm.abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == kPfMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                          smem_u32(&sm.tmem_base))
                      : "memory");
@@ -230,7 +240,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    if (warp == 4) {
+    if (warp == kPfProducerWarp) {
         // ------------------------------------------------------------ TMA producers
         // lane 0: Q, then the K ring; lane 1: the V ring (V tiles are needed
         // one softmax later than K tiles, so each ring runs at its own pace)
@@ -297,12 +307,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int j = issued > stages ? issued - stages : 0; j < issued; ++j)
                 mbar_wait(is_k ? &sm.k_full[j % stages] : &sm.v_full[j % stages], (j / stages) & 1);
         }
-    } else if (warp == 5) {
+    } else if (warp == kPfMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        // Order: S_0, S_1, then for each j: PV_j, S_{j+2}.  S_j lands in TMEM
-        // buffer j & 1 (columns 128 (j & 1) ..); the softmax writes P_j over
-        // it as fp16 and PV_j reads it from there, so S_{j+2} (same buffer)
-        // is issued after PV_j, and this thread's MMAs execute in order.
+        // Order: S_0, S_1, then for each j: PV_j (two halves), S_{j+2}.  S_j
+        // lands in TMEM buffer j & 1 (columns 128 (j & 1) ..); each softmax
+        // warpgroup writes its half of P_j (keys 64 w .. 64 w + 63) over the
+        // first 32 of its own 64 S columns, and the PV half
+        // w = P_j[:, half w] V_j[half w]
+        // accumulates into O_w (columns 256 + 128 w), so the two warpgroups
+        // never wait for each other; S_{j+2} (same buffer) is issued after
+        // both PV halves of j, and this thread's MMAs execute in order.
         if (lane == 0) {
             const uint32_t id_qk = umma_idesc(false), id_pv = umma_idesc(true);
             bool ok = pf_wait(sm, &sm.q_full, 0, p.status);
@@ -324,17 +338,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             if (ok && nk > 1) ok = issue_s(1);
             for (int j = 0; ok && j < nk; ++j) {
                 const int vs = j % kPfVStages;
-                if (!pf_wait(sm, &sm.p_full[j & 1], (j >> 1) & 1, p.status) ||
-                    !pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status))
-                    break;
-                tc_fence_after();
+                if (!pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status)) break;
+                for (int w = 0; w < 2 && ok; ++w) {
+                    if (!pf_wait(sm, &sm.p_full[w][j & 1], (j >> 1) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t bd = umma_desc(smem_u32(sm.v[vs][0]) + kk * 2048, kRegionBytes, 1024);
-                    umma_f16_ts(tmem + 256, tmem + 128 * (j & 1) + 8 * kk, bd, id_pv,
-                                (j > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 4 * w; kk < 4 * w + 4; ++kk) {
+                        const uint64_t bd = umma_desc(smem_u32(sm.v[vs][0]) + kk * 2048, kRegionBytes, 1024);
+                        // P half w sits in the first 32 of its own 64 S columns
+                        umma_f16_ts(tmem + 256 + 128 * w, tmem + 128 * (j & 1) + 32 * w + 8 * kk, bd,
+                                    id_pv, (j > 0 || kk > 4 * w) ? 1u : 0u);
+                    }
+                    umma_commit(&sm.pv_done[w][j & 1]);
                 }
-                umma_commit(&sm.pv_done[j & 1]);
+                if (!ok) break;
                 umma_commit(&sm.v_empty[vs]);
                 if (j + 2 < nk) ok = issue_s(j + 2);
             }
@@ -344,11 +364,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ softmax warps
-        const int t = threadIdx.x;  // query row within the tile
+        // Warpgroup w (warps 4w .. 4w + 3) takes key columns 64 w .. 64 w + 63
+        // of every tile for the query rows t = threadIdx.x % 128, with its own
+        // running max m_w, sum l_w and accumulator O_w; the two halves are
+        // combined once, in the epilogue.
+        const int t = threadIdx.x & 127;  // query row within the tile
+        const int wg = threadIdx.x >> 7;  // key half
         const int row_pos = p.start + q0 + t;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t o_col = 256 + 128 * wg;
         const float sc = p.scale_log2;
-        float m_run = -INFINITY, l = 0.f;  // running max (scaled, log2 domain) and sum
+        float m_run = -INFINITY, l = 0.f;  // running max (scaled, log2 domain) and sum of this half
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
             const int b = j & 1;
@@ -359,22 +385,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             tc_fence_after();
-            float sv[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + 128 * b + 32 * c, sv + 32 * c);
+            float sv[64];
+            tmem_ld32(lane_base + 128 * b + 64 * wg, sv);
+            tmem_ld32(lane_base + 128 * b + 64 * wg + 32, sv + 32);
             tmem_ld_wait();
-            const int k0 = 128 * j;
-            const int lim = row_pos - k0;  // keys c <= lim are visible to this row
-            if (lim < 127) {
+            const int k0 = 128 * j + 64 * wg;
+            const int lim = row_pos - k0;  // keys c <= lim of this half are visible to this row
+            if (lim < 63) {
 #pragma unroll
-                for (int c = 0; c < 128; ++c) sv[c] = c <= lim ? sv[c] : -INFINITY;
+                for (int c = 0; c < 64; ++c) sv[c] = c <= lim ? sv[c] : -INFINITY;
             }
-            // row max as a tree of eight independent chains
             float mx8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
 #pragma unroll
-            for (int c = 8; c < 128; c += 8)
+            for (int c = 8; c < 64; c += 8)
 #pragma unroll
                 for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], sv[c + e]);
 #pragma unroll
@@ -389,22 +414,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const bool grow = mt > m_run + 8.f;
             const float alpha = grow ? fast_exp2(m_run - mt) : 1.f;  // 0 when m_run = -inf
             if (j >= 1 && __any_sync(0xffffffffu, alpha < 1.f)) {
-                // O must be stable: P_{j-1} V_{j-1} has finished
-                if (!__all_sync(0xffffffffu,
-                                pf_wait(sm, &sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status))) {
+                // O_w must be stable: this half's P_{j-1} V_{j-1} has finished
+                if (!__all_sync(0xffffffffu, pf_wait(sm, &sm.pv_done[wg][(j - 1) & 1],
+                                                     ((j - 1) >> 1) & 1, p.status))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t oaddr = lane_base + 256;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float ov[32];
-                    tmem_ld32(oaddr + 32 * c, ov);
+                    tmem_ld32(lane_base + o_col + 32 * c, ov);
                     tmem_ld_wait();
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-                    tmem_st32(oaddr + 32 * c, ov);
+                    tmem_st32(lane_base + o_col + 32 * c, ov);
                 }
                 tmem_st_wait();
             }
@@ -412,80 +436,103 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 l *= alpha;
                 m_run = mt;
             }
-            // P_j = 2^(s * scale - m) as fp16 pairs over S_j's own columns:
-            // column c of this lane holds keys 2c (low half) and 2c + 1
-            const float nm = -m_run;
-            uint32_t pw[64];
+            // P = 2^(s * scale - m) as fp16 pairs over this half's own S
+            // columns (the other warpgroup may still be reading its columns):
+            // column 64 w + c of this lane holds keys 64 w + 2c (low half) and
+            // 64 w + 2c + 1.  A half with no visible key yet (m_run still
+            // -inf) writes zeros.
+            const float nm = m_run == -INFINITY ? 0.f : -m_run;
+            uint32_t pw[32];
             float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight partial sums
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
+            for (int c = 0; c < 32; ++c) {
                 const float p0 = fast_exp2(fmaf(sv[2 * c], sc, nm));
                 const float p1 = fast_exp2(fmaf(sv[2 * c + 1], sc, nm));
                 l8[c & 7] += p0 + p1;
                 pw[c] = pack_half2(p0, p1);
             }
             l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-            tmem_st32u(lane_base + 128 * b, pw);
-            tmem_st32u(lane_base + 128 * b + 32, pw + 32);
+            tmem_st32u(lane_base + 128 * b + 64 * wg, pw);
             tmem_st_wait();
-            if (k0 + 128 > kend) {
-                // V rows past the last needed key may hold stale bytes: zero
-                // this thread's row so 0 * garbage cannot reach O.
+            if (128 * j + 128 > kend) {
+                // V rows (keys) of this half past the last needed key may hold
+                // stale bytes: zero them so 0 * garbage cannot reach O_w
+                // (two threads per key row, one 128-byte head-dim half each).
                 const int vs = j % kPfVStages;
                 if (!__all_sync(0xffffffffu, pf_wait(sm, &sm.v_full[vs], (j / kPfVStages) & 1, p.status))) {
                     ok = false;
                     break;
                 }
-                if (k0 + t >= kend) {
+                const int key = 64 * wg + (t & 63), dh = t >> 6;
+                if (128 * j + key >= kend) {
 #pragma unroll
-                    for (int dh = 0; dh < 2; ++dh)
-#pragma unroll
-                        for (int ch = 0; ch < 8; ++ch)
-                            *reinterpret_cast<uint4*>(sm.v[vs][dh] + t * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<uint4*>(sm.v[vs][dh] + key * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
                 }
                 fence_proxy_async_smem();
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.p_full[b]);
+            if (lane == 0) mbar_arrive(&sm.p_full[wg][b]);
         }
+        // Both halves' last PV must have completed: each warpgroup combines
+        // O_0 and O_1 for its half of the head dims.
         const bool have_o = __all_sync(
-            0xffffffffu, ok && nk > 0 && pf_wait(sm, &sm.pv_done[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status));
-        // Epilogue: O / l goes through shared memory (the K ring is idle once
-        // the last PV has completed: every S MMA completed before it) so the
-        // global stores are coalesced.  Row t is staged at t * row_bytes with
-        // its 16-byte chunks permuted (chunk ^ (t & mask)) to spread banks.
+            0xffffffffu, ok && nk > 0 &&
+                             pf_wait(sm, &sm.pv_done[0][(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status) &&
+                             pf_wait(sm, &sm.pv_done[1][(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.status));
+        // Epilogue: the K ring is idle once the last PV has completed (every
+        // S MMA completed before it).  Each row's (m_w, l_w) go through K
+        // stage 2; O = (a_0 O_0 + a_1 O_1) / (a_0 l_0 + a_1 l_1) with
+        // a_w = 2^(m_w - max(m_0, m_1)) is staged through stages 0-1 (row t at
+        // t * row_bytes, 16-byte chunks permuted chunk ^ (t & mask) to spread
+        // banks) so the global stores are coalesced.
+        float2* ml = reinterpret_cast<float2*>(&sm.k[2][0][0]);  // [2][128]
+        ml[wg * 128 + t] = make_float2(m_run, l);
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
         const int row_bytes = p.out_f32 ? 512 : 256;
         const int chunks = row_bytes / 16, cmask = chunks - 1;
         uint8_t* stage = &sm.k[0][0][0];
         if (have_o) {
             tc_fence_after();
-            const float inv = 1.f / l;
+            const float2 ml0 = ml[t], ml1 = ml[128 + t];
+            const float m = fmaxf(ml0.x, ml1.x);
+            const float a0 = ml0.x == -INFINITY ? 0.f : fast_exp2(ml0.x - m);
+            const float a1 = ml1.x == -INFINITY ? 0.f : fast_exp2(ml1.x - m);
+            const float inv = 1.f / (a0 * ml0.y + a1 * ml1.y);
+            const float c0 = a0 * inv, c1 = a1 * inv;
             uint8_t* srow = stage + t * row_bytes;
-            float ov[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + 256 + 32 * c, ov + 32 * c);
+            float o0[64], o1[64];  // dims 64 wg .. 64 wg + 63 of O_0 and O_1
+            tmem_ld32(lane_base + 256 + 64 * wg, o0);
+            tmem_ld32(lane_base + 256 + 64 * wg + 32, o0 + 32);
+            tmem_ld32(lane_base + 384 + 64 * wg, o1);
+            tmem_ld32(lane_base + 384 + 64 * wg + 32, o1 + 32);
             tmem_ld_wait();
             if (p.out_f32) {
 #pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    *reinterpret_cast<float4*>(srow + 16 * (e ^ (t & cmask))) =
-                        make_float4(ov[4 * e] * inv, ov[4 * e + 1] * inv, ov[4 * e + 2] * inv,
-                                    ov[4 * e + 3] * inv);
+                for (int e = 0; e < 16; ++e) {
+                    const int ch = 16 * wg + e;  // 16-byte chunk of the row
+                    *reinterpret_cast<float4*>(srow + 16 * (ch ^ (t & cmask))) =
+                        make_float4(o0[4 * e] * c0 + o1[4 * e] * c1, o0[4 * e + 1] * c0 + o1[4 * e + 1] * c1,
+                                    o0[4 * e + 2] * c0 + o1[4 * e + 2] * c1, o0[4 * e + 3] * c0 + o1[4 * e + 3] * c1);
+                }
             } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    *reinterpret_cast<uint4*>(srow + 16 * (e ^ (t & cmask))) =
-                        make_uint4(pack_half2(ov[8 * e] * inv, ov[8 * e + 1] * inv),
-                                   pack_half2(ov[8 * e + 2] * inv, ov[8 * e + 3] * inv),
-                                   pack_half2(ov[8 * e + 4] * inv, ov[8 * e + 5] * inv),
-                                   pack_half2(ov[8 * e + 6] * inv, ov[8 * e + 7] * inv));
+                for (int e = 0; e < 8; ++e) {
+                    const int ch = 8 * wg + e;
+                    float x[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) x[u] = o0[8 * e + u] * c0 + o1[8 * e + u] * c1;
+                    *reinterpret_cast<uint4*>(srow + 16 * (ch ^ (t & cmask))) =
+                        make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]),
+                                   pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
+                }
             }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (have_o) {
             uint8_t* out = static_cast<uint8_t*>(p.out);
-            for (int u = t; u < rows_valid * chunks; u += 128) {
+            for (int u = threadIdx.x; u < rows_valid * chunks; u += 256) {
                 const int r = u / chunks, ch = u % chunks;
                 const uint4 val = *reinterpret_cast<const uint4*>(stage + r * row_bytes + 16 * (ch ^ (r & cmask)));
                 *reinterpret_cast<uint4*>(out + ((int64_t)(q0 + r) * p.hq + h) * row_bytes + 16 * ch) = val;
@@ -494,7 +541,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kPfMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
