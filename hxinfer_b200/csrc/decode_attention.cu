@@ -174,13 +174,29 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
     const int hkv = p.view.hkv;
     long long total = 0;
     bool odd = false;
-    // The first 32 sequences' lengths and ids are loaded together and kept,
-    // so a call of up to 32 sequences plans with one round of global loads.
-    const int len0 = lane < p.n_seqs ? p.lengths[lane] : 1;
-    const int sid0 = lane < p.n_seqs ? p.seq_ids[lane] : 0;
+    // The first kPlanRounds x 32 sequences' lengths and ids are loaded
+    // together and kept, so a call of up to 128 sequences plans with one
+    // round of global loads.
+    constexpr int kPlanRounds = 4;
+    int len_r[kPlanRounds], sid_r[kPlanRounds];
+#pragma unroll
+    for (int r = 0; r < kPlanRounds; ++r) {
+        const int s = 32 * r + lane;
+        len_r[r] = s < p.n_seqs ? p.lengths[s] : 1;
+        sid_r[r] = s < p.n_seqs ? p.seq_ids[s] : 0;
+    }
+    // the kept value of round base / 32, else a load (calls of more than 128 sequences)
+    auto kept = [&](const int (&arr)[kPlanRounds], int base, const int* src, int dflt) {
+        int v = dflt;
+#pragma unroll
+        for (int r = 0; r < kPlanRounds; ++r)
+            if (base == 32 * r) v = arr[r];
+        if (base >= 32 * kPlanRounds) v = base + lane < p.n_seqs ? src[base + lane] : dflt;
+        return v;
+    };
     for (int base = 0; base < p.n_seqs; base += 32) {
         const int s = base + lane;
-        const int len = base == 0 ? len0 : (s < p.n_seqs ? p.lengths[s] : 1);
+        const int len = kept(len_r, base, p.lengths, 1);
         odd |= len < 1 || len > p.view.capacity;
         int t = tiles_of(clamp_len(len, p.view.capacity)) * (s < p.n_seqs);
 #pragma unroll
@@ -214,9 +230,8 @@ __device__ void plan_cta(const DecodeParams& p, int cta, int grid, Smem& sm)
         int run = 0;  // tiles before the current chunk
         for (int base = 0; base < p.n_seqs; base += 32) {
             const int s = base + lane;
-            const int len = s < p.n_seqs
-                ? clamp_len(base == 0 ? len0 : p.lengths[s], p.view.capacity) : 0;
-            const int sid = base == 0 ? sid0 : (s < p.n_seqs ? p.seq_ids[s] : 0);
+            const int len = s < p.n_seqs ? clamp_len(kept(len_r, base, p.lengths, 1), p.view.capacity) : 0;
+            const int sid = kept(sid_r, base, p.seq_ids, 0);
             const int t = tiles_of(len) * hkv;
             int incl = t;
 #pragma unroll
