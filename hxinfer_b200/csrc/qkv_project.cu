@@ -202,18 +202,23 @@ __global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
     // each lane issues kBatch chunks x 4 rows (kBatch x 64 B) before it uses
     // any of them (for 1-2 tokens 128 KB per SM: 8 x 64 B x 256 threads in one
     // CTA, or 4 x 64 B x 256 threads in each of two).
-    constexpr int kBatch = BATCH;
-    for (int c0 = lane; c0 < chunks; c0 += 32 * kBatch) {
-        uint4 w[kBatch][4];
+    // Two buffers of BATCH / 2 chunks x 4 rows, used alternately: the next
+    // buffer's loads are issued before the current one is consumed, so a
+    // lane always has loads in flight (with one batch, issue-then-consume
+    // left the memory system idle while each batch was consumed).
+    constexpr int kHalf = BATCH / 2;
+    auto load = [&](uint4 (&w)[kHalf][4], int c0) {
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
+        for (int u = 0; u < kHalf; ++u) {
             const int c = c0 + 32 * u;
 #pragma unroll
             for (int r = 0; r < 4; ++r)  // read once: do not keep in L1/L2
                 w[u][r] = c < chunks ? __ldcs(wrow[r] + c) : make_uint4(0u, 0u, 0u, 0u);
         }
+    };
+    auto use = [&](const uint4 (&w)[kHalf][4], int c0) {
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
+        for (int u = 0; u < kHalf; ++u) {
             const int c = c0 + 32 * u;
             if (c >= chunks) break;
 #pragma unroll
@@ -225,6 +230,14 @@ __global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
                 }
             }
         }
+    };
+    uint4 wa[kHalf][4], wb[kHalf][4];
+    load(wa, lane);
+    for (int c0 = lane; c0 < chunks; c0 += 64 * kHalf) {
+        load(wb, c0 + 32 * kHalf);
+        use(wa, c0);
+        load(wa, c0 + 64 * kHalf);
+        use(wb, c0 + 32 * kHalf);
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r)
