@@ -135,7 +135,8 @@ __device__ __forceinline__ void qkv_epilogue(const KVView& view, const float (*r
     dst[d + 64] = __float2half_rn(x2);
 }
 
-// BATCH: weight chunks per lane in flight (see the main loop).  BATCH 8 holds
+// BATCH: weight chunks per lane held in registers, as two alternating
+// buffers of BATCH / 2 (see the main loop).  BATCH 8 holds
 // ~170 registers, one CTA per SM, for grids that fit the SMs in one wave;
 // BATCH <= 4 fits two CTAs per SM for larger grids.
 template <int NTOK, int BATCH, typename TP, typename TO>
@@ -198,14 +199,13 @@ __global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
 #pragma unroll
         for (int t = 0; t < NTOK; ++t) acc[r][t] = 0.f;
     // The weights are the only HBM traffic and one lane's arithmetic per chunk
-    // is small, so the loop is latency-bound unless many loads are in flight:
-    // each lane issues kBatch chunks x 4 rows (kBatch x 64 B) before it uses
-    // any of them (for 1-2 tokens 128 KB per SM: 8 x 64 B x 256 threads in one
-    // CTA, or 4 x 64 B x 256 threads in each of two).
-    // Two buffers of BATCH / 2 chunks x 4 rows, used alternately: the next
-    // buffer's loads are issued before the current one is consumed, so a
-    // lane always has loads in flight (with one batch, issue-then-consume
-    // left the memory system idle while each batch was consumed).
+    // is small, so the loop is latency-bound unless many loads are in flight.
+    // Two buffers of BATCH / 2 chunks x 4 rows (64 B per chunk), used
+    // alternately: the next buffer's loads are issued before the current one
+    // is consumed, so a lane always has loads in flight (for 1-2 tokens
+    // 64 KB per SM: 4 x 64 B x 256 threads in one CTA, or 2 x 64 B x 256
+    // threads in each of two).  With one batch issued and then consumed, the
+    // memory system idled while each batch was used.
     constexpr int kHalf = BATCH / 2;
     auto load = [&](uint4 (&w)[kHalf][4], int c0) {
 #pragma unroll
