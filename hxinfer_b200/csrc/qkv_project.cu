@@ -137,7 +137,7 @@ __device__ __forceinline__ void qkv_epilogue(const KVView& view, const float (*r
 
 // BATCH: weight chunks per lane held in registers, as two alternating
 // buffers of BATCH / 2 (see the main loop).  BATCH 8 holds
-// ~170 registers, one CTA per SM, for grids that fit the SMs in one wave;
+// ~200 registers, one CTA per SM, for grids that fit the SMs in one wave;
 // BATCH <= 4 fits two CTAs per SM for larger grids.
 template <int NTOK, int BATCH, typename TP, typename TO>
 __global__ void __launch_bounds__(kQkvThreads, BATCH >= 8 ? 1 : 2)
