@@ -690,3 +690,46 @@ def test_append_decode_refuses_other_head_sizes(hx):
     with pytest.raises(HXError):
         cache.append_decode(0, q, k, k.clone(), torch.zeros(1, dtype=torch.int32, device="cuda"),
                             torch.ones(1, dtype=torch.int32, device="cuda"), 4)
+
+
+def test_append_decode_under_programmatic_launch(hx):
+    """The one-launch step with HX_KV_OVERLAP_LAUNCH (each launch a
+    programmatic dependent of the previous one, as the benchmark runs it),
+    layer after layer and step after step on one stream, against K1 + K2 on
+    a copy: outputs and appended rows equal bit for bit."""
+    Hq, Hkv, hd, layers, steps = 32, 8, 128, 3, 3
+    lens = [int(x) for x in np.random.default_rng(8).integers(100, 2000, 64)]
+    n, cap = len(lens), max(lens) + steps + 1
+    caches = [hx.KVCache(layers, Hkv, hd, n, cap, overlap=ov) for ov in (False, True)]
+    for c in caches:
+        for s in range(n):
+            c.reserve(s, cap)
+        c.fill_normal(5)
+    table = hx.RopeTable(hd, cap, 5e5)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    sid = torch.arange(n, dtype=torch.int32, device="cuda")
+    qkv = [[tuple(torch.randn((n, m * hd), generator=g, device="cuda").half() for m in (Hq, Hkv, Hkv))
+            for _ in range(layers)] for _ in range(steps)]
+    ws = [torch.zeros(c.workspace_bytes(n, Hq), dtype=torch.uint8, device="cuda") for c in caches]
+    q_rot = torch.empty((n, Hq * hd), dtype=torch.float16, device="cuda")
+    want, got = [], []
+    for st in range(steps):
+        lengths = torch.tensor(lens, dtype=torch.int32, device="cuda") + st
+        for l in range(layers):
+            q, k, v = qkv[st][l]
+            caches[0].rope_append(l, k, v, sid, lengths - 1, q=q, num_q_heads=Hq, table=table,
+                                  q_out=q_rot)
+            want.append(caches[0].decode(l, q_rot, sid, lengths, Hq, workspace=ws[0]))
+            got.append(caches[1].append_decode(l, q, k, v, sid, lengths, Hq, table=table,
+                                               workspace=ws[1]))
+    torch.cuda.synchronize()
+    hx.device_status()
+    for i, (a, b) in enumerate(zip(want, got)):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16)), f"call {i}"
+    for l in range(layers):
+        for s in (0, 17, 63):
+            p0 = lens[s]
+            k0, v0 = caches[0].read(l, s, p0 - 1, steps)
+            k1, v1 = caches[1].read(l, s, p0 - 1, steps)
+            assert torch.equal(k0.view(torch.int16), k1.view(torch.int16))
+            assert torch.equal(v0.view(torch.int16), v1.view(torch.int16))
