@@ -60,6 +60,10 @@ def decode_case(a):
 
     def step(with_append):
         for l in range(layers):
+            if with_append == "one_launch":
+                cache.append_decode(l, q[l], k[l], v[l], sid, lens, hq, table=table, out=out[l],
+                                    workspace=ws, stream=stream)
+                continue
             if with_append:
                 cache.rope_append(l, k[l], v[l], sid, pos, q=q[l], num_q_heads=hq, table=table,
                                   q_out=q_rot[l], stream=stream)
@@ -68,8 +72,9 @@ def decode_case(a):
     res = {}
     with torch.cuda.stream(stream):
         step(True)  # warm-up (sets kernel attributes outside capture)
+        step("one_launch")
         torch.cuda.synchronize()
-        for name, app in (("step", True), ("decode_only", False)):
+        for name, app in (("step", True), ("decode_only", False), ("one_launch", "one_launch")):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 step(app)
@@ -87,6 +92,7 @@ def decode_case(a):
                       "overlap": a.overlap,
                       "graph_us_per_layer_step": 1e3 * res["step"],
                       "graph_us_per_layer_decode": 1e3 * res["decode_only"],
+                      "graph_us_per_layer_one_launch_step": 1e3 * res["one_launch"],
                       "bytes_per_launch": nbytes,
                       "decode_gbs": nbytes / (res["decode_only"] * 1e-3) / 1e9,
                       "step_gbs": nbytes / (res["step"] * 1e-3) / 1e9}))
@@ -198,14 +204,24 @@ def c2_case(a):
                 cache.decode(l, qd_rot[t], sid, len_tab[t], hq, out=out_d[t], workspace=ws,
                              stream=stream)
 
+    def decode_all_one_launch():  # the same steps, one hx_append_decode_attention each
+        for t in range(steps):
+            for l in range(layers):
+                cache.append_decode(l, qd[t], kd[t], vd[t], sid, len_tab[t], hq, table=table,
+                                    out=out_d[t], workspace=ws, stream=stream)
+
     with torch.cuda.stream(stream):
         prefill()
         decode_all()  # warm-up, sets kernel attributes outside capture
+        decode_all_one_launch()
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             decode_all()
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        graph1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph1, stream=stream):
+            decode_all_one_launch()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         e[0].record(stream)
         prefill()
         e[1].record(stream)
@@ -213,10 +229,15 @@ def c2_case(a):
         e[2].record(stream)
         graph.replay()
         e[3].record(stream)
+        graph1.replay()
+        e[4].record(stream)
+        graph1.replay()
+        e[5].record(stream)
         torch.cuda.synchronize()
     kv.device_status()
     pre_ms = e[0].elapsed_time(e[1])
     dec_ms = e[2].elapsed_time(e[3])
+    dec1_ms = e[4].elapsed_time(e[5])
     pairs = n0 * (n0 + 1) // 2
     pre_flops = 4.0 * hq * hd * pairs * layers
     dec_bytes = 2.0 * hkv * hd * 2 * sum(range(n0 + 1, n0 + steps + 1)) * layers
@@ -224,6 +245,7 @@ def c2_case(a):
                       "layers": layers, "prefill_ms": pre_ms,
                       "prefill_tflops_incl_append": pre_flops / (pre_ms * 1e-3) / 1e12,
                       "decode_ms": dec_ms, "decode_us_per_step_layer": 1e3 * dec_ms / (steps * layers),
+                      "one_launch_decode_us_per_step_layer": 1e3 * dec1_ms / (steps * layers),
                       "decode_kv_bytes": dec_bytes,
                       "decode_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9}))
 
