@@ -317,18 +317,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // accumulates into O_w (columns 256 + 128 w), so the two warpgroups
         // never wait for each other; S_{j+2} (same buffer) is issued after
         // both PV halves of j, and this thread's MMAs execute in order.
+        // The shared-memory descriptors are built once: an operand's start
+        // address sits in the low 14 bits as address / 16, and every address
+        // here is below 256 KB, so moving to another K slice, region or ring
+        // stage adds a constant (bytes / 16) without a carry out of the
+        // field.  Each MMA then costs this thread one add, not a rebuild,
+        // which matters because this warp shares its issue slots with two
+        // softmax warps.
         if (lane == 0) {
             const uint32_t id_qk = umma_idesc(false), id_pv = umma_idesc(true);
+            const uint64_t q_desc = umma_desc(smem_u32(sm.q[0]), 16, 1024);
+            const uint64_t k_desc = umma_desc(smem_u32(sm.k[0][0]), 16, 1024);
+            const uint64_t v_desc = umma_desc(smem_u32(sm.v[0][0]), kRegionBytes, 1024);
+            constexpr uint64_t kStageStep = (2 * kRegionBytes) >> 4;  // one ring stage
             bool ok = pf_wait(sm, &sm.q_full, 0, p.status);
             auto issue_s = [&](int j) {
                 const int ks = j % kPfKStages;
                 if (!pf_wait(sm, &sm.k_full[ks], (j / kPfKStages) & 1, p.status)) return false;
                 tc_fence_after();
+                const uint64_t kd = k_desc + (uint64_t)ks * kStageStep;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t a = umma_desc(smem_u32(sm.q[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = umma_desc(smem_u32(sm.k[ks][kk >> 2]) + (kk & 3) * 32, 16, 1024);
-                    umma_f16(tmem + 128 * (j & 1), a, bd, id_qk, kk > 0);
+                    // K slice kk: region kk / 4, 32 bytes (16 fp16) apart within it
+                    const uint64_t off = (uint64_t)(((kk >> 2) * kRegionBytes + (kk & 3) * 32) >> 4);
+                    umma_f16(tmem + 128 * (j & 1), q_desc + off, kd + off, id_qk, kk > 0);
                 }
                 umma_commit(&sm.s_full[j & 1]);
                 umma_commit(&sm.k_empty[ks]);
@@ -345,9 +357,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         break;
                     }
                     tc_fence_after();
+                    const uint64_t vd = v_desc + (uint64_t)vs * kStageStep;
 #pragma unroll
                     for (int kk = 4 * w; kk < 4 * w + 4; ++kk) {
-                        const uint64_t bd = umma_desc(smem_u32(sm.v[vs][0]) + kk * 2048, kRegionBytes, 1024);
+                        const uint64_t bd = vd + (uint64_t)((kk * 2048) >> 4);  // 16 keys = 2048 bytes
                         // P half w sits in the first 32 of its own 64 S columns
                         umma_f16_ts(tmem + 256 + 128 * w, tmem + 128 * (j & 1) + 32 * w + 8 * kk, bd,
                                     id_pv, (j > 0 || kk > 4 * w) ? 1u : 0u);

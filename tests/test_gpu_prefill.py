@@ -106,3 +106,27 @@ def test_prefill_rows_rescale_apart(hx, oracle, out_dtype):
     vc = rng.standard_normal((n, Hkv, 128))
     qkv = tuple(oracle.f16(a.reshape(a.shape[0], -1)) for a in (q, kc, vc))
     run_prefill(hx, oracle, Hq, Hkv, 0, n, seed=0, out_dtype=out_dtype, qkv=qkv)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_prefill_writes_only_its_rows(hx, oracle, out_dtype):
+    """The output tile is written by tensor-map stores clipped at row n: the
+    last, partial query tile leaves the caller's rows past n untouched, and
+    an output that starts one row into a buffer leaves the row before it."""
+    Hq, Hkv, n = 4, 2, 77
+    rng = np.random.default_rng(21)
+    kc = oracle.f16(rng.standard_normal((n, Hkv * 128)))
+    vc = oracle.f16(rng.standard_normal((n, Hkv * 128)))
+    q = oracle.f16(rng.standard_normal((n, Hq * 128)))
+    cache = hx.KVCache(1, Hkv, 128, 1, n)
+    cache.reserve(0, n)
+    cache.write(0, 0, 0, torch.from_numpy(kc).half().cuda(), torch.from_numpy(vc).half().cuda())
+    buf = torch.full((n + 130, Hq * 128), 7.0, dtype=out_dtype, device="cuda")
+    cache.prefill(0, torch.from_numpy(q).half().cuda(), 0, 0, Hq, scale=1.0 / math.sqrt(128),
+                  out=buf[1:n + 1])
+    torch.cuda.synchronize()
+    hx.device_status()
+    assert bool((buf[0] == 7.0).all()) and bool((buf[n + 1:] == 7.0).all())
+    want = oracle.prefill_attention(q, kc, vc, 0, Hq, Hkv, 128)
+    got = buf[1:n + 1].float().cpu().numpy()
+    assert np.all(np.abs(got - want) <= ATOL + RTOL * np.abs(want))
