@@ -3,6 +3,7 @@
     python -m hxinfer_b200.profile_case decode  --shape llama3 --seqs 16 --len 8192 --layers 1 --iters 5
     python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --len 16874 --layers 8 --iters 20
+    python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --ragged --layers 8 --iters 20 --overlap
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
@@ -39,6 +40,10 @@ def decode_case(a):
     RoPE+append (K1) then the split-K decode (K2); also K2 alone."""
     hq, hkv, theta = SHAPES[a.shape]
     hd, n, L, layers = 128, a.seqs, a.len, a.layers
+    if a.ragged:  # the batched decode workload's lengths: U[512, 32768], seed 20261201
+        import numpy as np
+        lens_h = np.random.default_rng(20261201).integers(512, 32769, n).astype(np.int64)
+        L = int(lens_h.max())
     cap = L + 2
     cache = kv.KVCache(layers, hkv, hd, n, cap, overlap=a.overlap)
     for s in range(n):
@@ -54,8 +59,12 @@ def decode_case(a):
     out = torch.empty_like(q)
     sid = torch.arange(n, dtype=torch.int32, device="cuda")
     ws = torch.zeros(cache.workspace_bytes(n, hq), dtype=torch.uint8, device="cuda")
-    pos = torch.full((n,), L - 1, dtype=torch.int32, device="cuda")
-    lens = pos + 1
+    if a.ragged:
+        lens = torch.tensor(lens_h, dtype=torch.int32, device="cuda")
+        pos = lens - 1
+    else:
+        pos = torch.full((n,), L - 1, dtype=torch.int32, device="cuda")
+        lens = pos + 1
     stream = torch.cuda.Stream()
 
     def step(with_append):
@@ -87,8 +96,9 @@ def decode_case(a):
             torch.cuda.synchronize()
             res[name] = e0.elapsed_time(e1) / (a.iters * layers)
     kv.device_status()
-    nbytes = 2 * n * L * hkv * hd * 2
-    print(json.dumps({"case": "decode", "shape": a.shape, "seqs": n, "len": L, "layers": layers,
+    nbytes = 2 * int(lens.sum().item()) * hkv * hd * 2
+    print(json.dumps({"case": "decode", "shape": a.shape, "seqs": n,
+                      "len": "U[512,32768]" if a.ragged else L, "layers": layers,
                       "overlap": a.overlap,
                       "graph_us_per_layer_step": 1e3 * res["step"],
                       "graph_us_per_layer_decode": 1e3 * res["decode_only"],
@@ -581,6 +591,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1024, help="c2, c5: decode steps after the prompt")
     ap.add_argument("--new", type=int, default=256, help="c5: tokens prefilled after the restored prefix")
     ap.add_argument("--conts", type=int, default=32, help="c5: continuations of the prefix")
+    ap.add_argument("--ragged", action="store_true",
+                    help="decode: lengths U[512, 32768] (seed 20261201), as the batched bench")
     ap.add_argument("--overlap", action="store_true",
                     help="programmatic dependent launch of append -> decode (HX_KV_OVERLAP_LAUNCH)")
     a = ap.parse_args()
