@@ -280,11 +280,13 @@ def run_batched_decode(args):
         # to the peers; a step ends when its last exchange has completed.
         side = torch.cuda.Stream()
 
-    def attend(l, si, q, k, v, timed_events=False):
+    def attend(l, si, q, k, v, timed_events=False, out_buf=None):
         """One layer of a decode step: the new tokens' RoPE + append and the
         decode attention, in one launch (hx_append_decode_attention), or with
-        --separate as K1 then K2 (hx_rope_append, hx_decode_attention)."""
+        --separate as K1 then K2 (hx_rope_append, hx_decode_attention).
+        Without the gather the rows go to out_buf (default `out`)."""
         pos, lens = pos_tab[si], len_tab[si]
+        o = out if out_buf is None else out_buf
         if args.separate:
             cache.rope_append(l, k, v, seq_ids, pos, q=q, num_q_heads=hq, table=table,
                               q_out=q_rot[l])
@@ -301,9 +303,9 @@ def run_batched_decode(args):
             else:
                 cache.append_decode_gather(l, q, k, v, seq_ids, lens, hq, peer, table=table, **place)
         elif args.separate:
-            cache.decode(l, q_rot[l], seq_ids, lens, hq, out=out[l], workspace=ws)
+            cache.decode(l, q_rot[l], seq_ids, lens, hq, out=o[l], workspace=ws)
         else:
-            cache.append_decode(l, q, k, v, seq_ids, lens, hq, table=table, out=out[l],
+            cache.append_decode(l, q, k, v, seq_ids, lens, hq, table=table, out=o[l],
                                 workspace=ws)
         if timed_events:
             e1.record(stream)
@@ -314,7 +316,7 @@ def run_batched_decode(args):
             side.wait_event(done)
             peer.wait(epoch[0], stream=side)
         elif world > 1:
-            dist.all_gather_into_tensor(gathered[l], out[l])
+            dist.all_gather_into_tensor(gathered[l], o[l])
     seq_ids = torch.arange(n, dtype=torch.int32, device=dev)
     total_steps = W + 2 * K
     base = torch.from_numpy(my_len.astype(np.int32)).to(dev)
@@ -389,7 +391,12 @@ def run_batched_decode(args):
     achieved = dec_bytes / (dec_avg_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
 
-    # ---- end to end: host (pinned) q/k/v in, attention outputs out, every step
+    # ---- end to end: host (pinned) q/k/v in, attention outputs out, every step.
+    # Served as a pipeline: device inputs and (without the gather) outputs are
+    # double-buffered, and a copy stream uploads step i+1's inputs and reads
+    # back step i's outputs while the neighbouring step computes.  With the
+    # gather the read-back stays on the compute stream after the step's
+    # exchange, since peers write the same gather region again two steps on.
     q_h = q_in.cpu().pin_memory()
     k_h = k_in.cpu().pin_memory()
     v_h = v_in.cpu().pin_memory()
@@ -399,26 +406,52 @@ def run_batched_decode(args):
         out_h = torch.empty((LAYERS, r1 - r0, HQ * HD), dtype=torch.float16).pin_memory()
     else:
         out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d, k_d, v_d = torch.empty_like(q_in), torch.empty_like(k_in), torch.empty_like(v_in)
+    q_d = [torch.empty_like(q_in) for _ in range(2)]
+    k_d = [torch.empty_like(k_in) for _ in range(2)]
+    v_d = [torch.empty_like(v_in) for _ in range(2)]
+    outs = [out, torch.empty_like(out)]
+    copy = torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step(si):
-        q_d.copy_(q_h, non_blocking=True)
-        k_d.copy_(k_h, non_blocking=True)
-        v_d.copy_(v_h, non_blocking=True)
+    def upload(i):
+        """Inputs of the i-th end-to-end step into buffer i % 2 (copy stream),
+        once step i - 2 has finished reading that buffer."""
+        b = i % 2
+        if i >= 2:
+            copy.wait_event(ev_done[b])
+        with torch.cuda.stream(copy):
+            q_d[b].copy_(q_h, non_blocking=True)
+            k_d[b].copy_(k_h, non_blocking=True)
+            v_d[b].copy_(v_h, non_blocking=True)
+        ev_in[b].record(copy)
+
+    def e2e_step(i, si):
+        b = i % 2
+        stream.wait_event(ev_in[b])
         for l in range(LAYERS):
-            attend(l, si, q_d[l], k_d[l], v_d[l])
+            attend(l, si, q_d[b][l], k_d[b][l], v_d[b][l], out_buf=outs[b])
         if p2p:
             stream.wait_stream(side)
             out_h.copy_(assembled[si % 2, :, r0:r1], non_blocking=True)
+            ev_done[b].record(stream)
         else:
-            out_h.copy_(out, non_blocking=True)
+            ev_done[b].record(stream)
+            copy.wait_event(ev_done[b])
+            with torch.cuda.stream(copy):
+                out_h.copy_(outs[b], non_blocking=True)
 
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for s in range(W + K, W + 2 * K):
-        e2e_step(s)
+    copy.wait_event(e0)
+    upload(0)
+    for i, s in enumerate(range(W + K, W + 2 * K)):
+        if i + 1 < K:
+            upload(i + 1)
+        e2e_step(i, s)
+    stream.wait_stream(copy)
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -471,7 +504,10 @@ def run_batched_decode(args):
             "hbm_gbs_step": float(2 * (lengths.sum() + NSEQ) * HKV * HD * 2 * LAYERS) / (ms / K * 1e-3) / 1e9,
             "cpu_baseline": cpu,
             "e2e": {"value": NSEQ * K / (e2e_ms * 1e-3), "unit": "tok/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "copies": ("pinned host buffers; uploads " + ("and read-backs " if not p2p else "")
+                               + "on a second stream, double-buffered, overlapping the "
+                               "neighbouring step's compute")},
             "gpu_launches": K * LAYERS * ((1 if args.separate else 0)
                                           + kv.decode_kernel_count(n * hkv, HD, HQ // HKV)
                                           + (1 if p2p else 0)),
