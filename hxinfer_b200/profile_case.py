@@ -3,7 +3,7 @@
     python -m hxinfer_b200.profile_case decode  --shape llama3 --seqs 16 --len 8192 --layers 1 --iters 5
     python -m hxinfer_b200.profile_case decode  --shape qwen   --seqs 1  --len 32769 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --len 16874 --layers 8 --iters 20
-    python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --ragged --layers 8 --iters 20 --overlap
+    python -m hxinfer_b200.profile_case decode  --shape llama3_kvhead --seqs 64 --ragged --layers 8 --iters 20 --overlap --gather
     python -m hxinfer_b200.profile_case snapshot --shape qwen  --len 2048 --layers 28 --iters 20
     python -m hxinfer_b200.profile_case prefill --shape llama2 --len 1024 --layers 4 --iters 5
     python -m hxinfer_b200.profile_case c2 --len 1024 --steps 1024 --layers 1
@@ -67,8 +67,22 @@ def decode_case(a):
         lens = pos + 1
     stream = torch.cuda.Stream()
 
+    gather = None
+    if a.gather:
+        # a one-rank gather endpoint: the gathering kernels store the rows into
+        # this rank's own buffer, which isolates their cost from the exchange
+        row_bytes = hq * hd * 2
+        gather = kv.PeerGather(0, 1, 2 * n * row_bytes, lambda b: [b])
+        g_rows = torch.arange(n, dtype=torch.int32, device="cuda")
+
     def step(with_append):
         for l in range(layers):
+            if with_append == "one_launch_gather":
+                cache.append_decode_gather(l, q[l], k[l], v[l], sid, lens, hq, gather,
+                                           out_offset=(l & 1) * n * row_bytes, out_rows=g_rows,
+                                           out_row_heads=hq, out_head0=0, table=table,
+                                           workspace=ws, stream=stream)
+                continue
             if with_append == "one_launch":
                 cache.append_decode(l, q[l], k[l], v[l], sid, lens, hq, table=table, out=out[l],
                                     workspace=ws, stream=stream)
@@ -82,8 +96,13 @@ def decode_case(a):
     with torch.cuda.stream(stream):
         step(True)  # warm-up (sets kernel attributes outside capture)
         step("one_launch")
+        if gather is not None:
+            step("one_launch_gather")
         torch.cuda.synchronize()
-        for name, app in (("step", True), ("decode_only", False), ("one_launch", "one_launch")):
+        kinds = [("step", True), ("decode_only", False), ("one_launch", "one_launch")]
+        if gather is not None:
+            kinds.append(("one_launch_gather", "one_launch_gather"))
+        for name, app in kinds:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 step(app)
@@ -96,6 +115,8 @@ def decode_case(a):
             torch.cuda.synchronize()
             res[name] = e0.elapsed_time(e1) / (a.iters * layers)
     kv.device_status()
+    if gather is not None:
+        gather.close()
     nbytes = 2 * int(lens.sum().item()) * hkv * hd * 2
     print(json.dumps({"case": "decode", "shape": a.shape, "seqs": n,
                       "len": "U[512,32768]" if a.ragged else L, "layers": layers,
@@ -103,6 +124,8 @@ def decode_case(a):
                       "graph_us_per_layer_step": 1e3 * res["step"],
                       "graph_us_per_layer_decode": 1e3 * res["decode_only"],
                       "graph_us_per_layer_one_launch_step": 1e3 * res["one_launch"],
+                      "graph_us_per_layer_one_launch_gather_world1":
+                          1e3 * res["one_launch_gather"] if gather is not None else None,
                       "bytes_per_launch": nbytes,
                       "decode_gbs": nbytes / (res["decode_only"] * 1e-3) / 1e9,
                       "step_gbs": nbytes / (res["step"] * 1e-3) / 1e9}))
@@ -591,6 +614,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1024, help="c2, c5: decode steps after the prompt")
     ap.add_argument("--new", type=int, default=256, help="c5: tokens prefilled after the restored prefix")
     ap.add_argument("--conts", type=int, default=32, help="c5: continuations of the prefix")
+    ap.add_argument("--gather", action="store_true",
+                    help="decode: also time the gathering one-launch step with a one-rank endpoint")
     ap.add_argument("--ragged", action="store_true",
                     help="decode: lengths U[512, 32768] (seed 20261201), as the batched bench")
     ap.add_argument("--overlap", action="store_true",
