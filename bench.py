@@ -60,10 +60,10 @@ EVENT_STRIDE = 4
 METRIC = "decode tok/s (batched decode attention)"
 # DRAM bytes (read + write) of one decode launch / its algorithmic bytes,
 # from an ncu capture of the same kernel on 16 sequences x 8192 positions
-# (540.6 MB of DRAM traffic for 537.0 MB of K+V+q+out); the traffic of the
+# (541.6 MB of DRAM traffic for 537.1 MB of K+V+q+out); the traffic of the
 # bench's 4.4 GB launches scales with the tiles read, so `roofline.traffic`
 # is this ratio times the launch's algorithmic bytes.
-DECODE_TRAFFIC_RATIO = 1.007
+DECODE_TRAFFIC_RATIO = 1.008
 
 
 def lengths_c4():
