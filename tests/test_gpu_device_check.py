@@ -25,6 +25,8 @@ def test_calls_from_another_device_are_refused():
         buf = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda:0")
         torch.cuda.synchronize()
     d = P(buf.data_ptr())
+    spec = _lib.hx_append_spec(k=d.value, v=d.value, bq=None, bk=None, bv=None,
+                               dtype=_lib.HX_FP16, table=table.handle)
     with torch.cuda.device(1):
         s = P(torch.cuda.current_stream().cuda_stream)
         calls = {
@@ -46,6 +48,9 @@ def test_calls_from_another_device_are_refused():
                 buf.numel(), s),
             "hx_decode_attention_noalloc": lambda: lib.hx_decode_attention_noalloc(
                 cache.handle, 0, d, _lib.HX_FP16, d, d, 1, 28, 0.1, d, _lib.HX_FP16, s),
+            "hx_append_decode_attention": lambda: lib.hx_append_decode_attention(
+                cache.handle, 0, d, C.byref(spec), d, d, 1, 28, 0.1, d, _lib.HX_FP16, d,
+                buf.numel(), s),
             "hx_prefill_attention": lambda: lib.hx_prefill_attention(
                 cache.handle, 0, d, 0, 0, 16, 28, 0.1, d, _lib.HX_FP16, s),
             "hx_kv_snapshot": lambda: lib.hx_kv_snapshot(cache.handle, 0, 64, d, buf.numel(), s),
