@@ -409,7 +409,7 @@ def run_batched_decode(args):
     q_d = [torch.empty_like(q_in) for _ in range(2)]
     k_d = [torch.empty_like(k_in) for _ in range(2)]
     v_d = [torch.empty_like(v_in) for _ in range(2)]
-    outs = [out, torch.empty_like(out)]
+    outs = [out, torch.zeros_like(out)]  # padding rows read back as zeros in both
     copy = torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
