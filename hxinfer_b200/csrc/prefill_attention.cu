@@ -321,9 +321,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // address sits in the low 14 bits as address / 16, and every address
         // here is below 256 KB, so moving to another K slice, region or ring
         // stage adds a constant (bytes / 16) without a carry out of the
-        // field.  Each MMA then costs this thread one add, not a rebuild,
-        // which matters because this warp shares its issue slots with two
-        // softmax warps.
+        // field.  Each MMA then costs this thread one add, not a rebuild
+        // (this warp shares its issue slots with two softmax warps).
         if (lane == 0) {
             const uint32_t id_qk = umma_idesc(false), id_pv = umma_idesc(true);
             const uint64_t q_desc = umma_desc(smem_u32(sm.q[0]), 16, 1024);
